@@ -1,0 +1,163 @@
+/*
+ * megaqwen_b200.h -- C ABI of the B200 (sm_100a) Qwen3-0.6B decode engine.
+ *
+ * Drop-in for the extern "C" launchers of Infatoshi/MegaQwen's torch
+ * extension.  Every pointer argument is a plain device pointer unless stated;
+ * no torch types cross this boundary.  Tensors use the reference layouts:
+ *   weights     bf16, row-major [out_features, in_features] (HF nn.Linear)
+ *   embed/lm    bf16 [151936, 1024] (lm_head may alias embed: tied)
+ *   cos/sin     bf16 [max_seq_len, 128] (halves duplicated)
+ *   k/v cache   bf16 [num_layers, 8, max_seq_len, 128] contiguous
+ *
+ * Reference interfaces replaced (file:line inside the MegaQwen tree):
+ *   LDGLayerWeights               csrc/megakernel/fused_decode_ldg.cu:24-36
+ *   launch_ldg_decode             csrc/megakernel/fused_decode_ldg.cu:893-969
+ *   launch_ldg_decode_with_logits csrc/megakernel/fused_decode_ldg.cu:972-1057
+ *   launch_prefill_float          csrc/megakernel/fused_prefill.cu:601-867
+ */
+#ifndef MEGAQWEN_B200_H
+#define MEGAQWEN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Model constants (Qwen3-0.6B; csrc/megakernel/config.cuh:33-40). */
+#define MQ_HIDDEN_SIZE 1024
+#define MQ_INTERMEDIATE_SIZE 3072
+#define MQ_NUM_Q_HEADS 16
+#define MQ_NUM_KV_HEADS 8
+#define MQ_HEAD_DIM 128
+#define MQ_VOCAB_SIZE 151936
+#define MQ_MAX_LAYERS 63
+
+/* Per-layer weight pointers, same field order and size as the reference's
+ * LDGLayerWeights (fused_decode_ldg.cu:24-36) and PrefillLayerWeights
+ * (fused_prefill.cu:28-40). */
+typedef struct LDGLayerWeights {
+    const void* input_layernorm_weight;
+    const void* q_proj_weight;
+    const void* k_proj_weight;
+    const void* v_proj_weight;
+    const void* q_norm_weight;
+    const void* k_norm_weight;
+    const void* o_proj_weight;
+    const void* post_attn_layernorm_weight;
+    const void* gate_proj_weight;
+    const void* up_proj_weight;
+    const void* down_proj_weight;
+} LDGLayerWeights;
+
+typedef LDGLayerWeights PrefillLayerWeights;
+
+/* Status codes (0 = success). */
+enum {
+    MQ_OK = 0,
+    MQ_ERR_INVALID_ARGUMENT = 1,   /* bad size, position, token, null pointer */
+    MQ_ERR_WAIT_TIMEOUT = 2,       /* an inter-CTA handoff wait ran out of time */
+    MQ_ERR_PIPE_TIMEOUT = 3,       /* a shared-memory pipeline wait ran out of time */
+    MQ_ERR_BAD_TOKEN = 4,          /* input token outside [0, vocab) (device check) */
+    MQ_ERR_BAD_POSITION = 5,       /* position outside [0, max_seq_len) (device check) */
+    MQ_ERR_CUDA = 6,               /* a CUDA runtime call failed */
+    MQ_ERR_WORKSPACE = 7           /* workspace missing or too small */
+};
+
+/* ---- reference ABI -------------------------------------------------------
+ * launch_ldg_decode: one batch-1 decode step; replaces fused_decode_ldg.cu:893.
+ * Same 27 arguments.  layer_weights is a DEVICE array of num_layers structs.
+ * Writes the greedy next token to output_token_id (device int32), the K/V rows
+ * of `position` into the caches, the final bf16 hidden state (before the final
+ * norm) into hidden_buffer and the final-normed fp32 hidden into g_normalized.
+ * g_activations, g_residual, g_q, g_k, g_v, g_attn_out, g_mlp_intermediate,
+ * block_max_vals and block_max_idxs are accepted and not used: the engine
+ * keeps its inter-CTA state in a per-device workspace allocated on the first
+ * call on each device.  cache_len must equal position + 1.  Returns nothing,
+ * like the reference; mq_get_last_error() reports the launch status.        */
+void launch_ldg_decode(int input_token_id, int* output_token_id, const void* embed_weight,
+                       const LDGLayerWeights* layer_weights, const void* final_norm_weight,
+                       const void* lm_head_weight, const void* cos_table, const void* sin_table, void* k_cache,
+                       void* v_cache, void* hidden_buffer, void* g_activations, void* g_residual, void* g_q,
+                       void* g_k, void* g_v, void* g_attn_out, void* g_mlp_intermediate, void* g_normalized,
+                       void* block_max_vals, void* block_max_idxs, int num_layers, int position, int cache_len,
+                       int max_seq_len, float attn_scale, cudaStream_t stream);
+
+/* launch_ldg_decode_with_logits: as above, plus the full fp32 logits
+ * [151936] into logits_output; replaces fused_decode_ldg.cu:972-1057.       */
+void launch_ldg_decode_with_logits(int input_token_id, int* output_token_id, float* logits_output,
+                                   const void* embed_weight, const LDGLayerWeights* layer_weights,
+                                   const void* final_norm_weight, const void* lm_head_weight, const void* cos_table,
+                                   const void* sin_table, void* k_cache, void* v_cache, void* hidden_buffer,
+                                   void* g_activations, void* g_residual, void* g_q, void* g_k, void* g_v,
+                                   void* g_attn_out, void* g_mlp_intermediate, void* g_normalized,
+                                   void* block_max_vals, void* block_max_idxs, int num_layers, int position,
+                                   int cache_len, int max_seq_len, float attn_scale, cudaStream_t stream);
+
+/* ---- native API ------------------------------------------------------------
+ * The decode step with an explicit, caller-owned workspace and an explicit
+ * status.  Extends launch_ldg_decode (fused_decode_ldg.cu:893-921) with:
+ *   - input token from device memory (input_token_ptr; greedy feedback when it
+ *     equals output_token) and, optionally, position from device memory
+ *     (position_ptr, advanced by one on success) so steps can be replayed
+ *     without host round trips;
+ *   - an error word in the workspace written by bounded device-side waits.  */
+typedef struct mq_decode_params {
+    int input_token;               /* used when input_token_ptr is NULL */
+    const int* input_token_ptr;    /* device int32, optional */
+    int* output_token;             /* device int32, optional */
+    float* logits;                 /* device fp32 [151936], optional */
+    const void* embed;
+    const LDGLayerWeights* layers; /* device array [num_layers] */
+    const void* final_norm;
+    const void* lm_head;
+    const void* cos_table;
+    const void* sin_table;
+    void* k_cache;
+    void* v_cache;
+    void* hidden_out;              /* device bf16 [1024], optional */
+    float* normalized_out;         /* device fp32 [1024], optional */
+    void* workspace;               /* device, mq_decode_workspace_bytes() bytes, zeroed once */
+    size_t workspace_bytes;
+    int num_layers;
+    int position;                  /* used when position_ptr is NULL */
+    int* position_ptr;             /* device int32, optional; incremented on success */
+    int max_seq_len;
+    float attn_scale;
+    int num_ctas;                  /* 0: one CTA per SM */
+    int attn_chunk;                /* target KV positions per attention work unit; 0: default */
+    long long timeout_ns;          /* bound on every device wait; 0: default (2 s) */
+    int inject_skip_cta;           /* test hook: CTA (value - 1) withholds its layer-0 QKV handoff
+                                      stores, so the others' waits run out; 0: off */
+} mq_decode_params;
+
+size_t mq_decode_workspace_bytes(void);
+/* Zero a workspace (stream-ordered).  Needed once before first use and after
+ * any call that returned an error. */
+int mq_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream);
+/* Launch one decode step.  Host-side argument checks return an error code
+ * without launching; device-side failures land in the workspace error word. */
+int mq_decode(const mq_decode_params* params, cudaStream_t stream);
+/* Copy the workspace error word (and the auxiliary info word) to the host;
+ * synchronises `stream`. */
+int mq_decode_read_error(const void* workspace, uint32_t* error, uint32_t* info, cudaStream_t stream);
+/* Copy the step result from the workspace to the host and synchronise
+ * `stream`: the greedy token of the last successful step, the error word and
+ * the auxiliary info word.  One 32-byte device-to-host copy. */
+int mq_decode_fetch(const void* workspace, int* token, uint32_t* error, uint32_t* info, cudaStream_t stream);
+/* Number of CTAs the decode kernel would use on the current device. */
+int mq_decode_default_ctas(void);
+
+/* Last status recorded by the reference-ABI launchers on this host thread. */
+int mq_get_last_error(void);
+const char* mq_error_string(int code);
+/* Library version string. */
+const char* mq_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MEGAQWEN_B200_H */

@@ -1,0 +1,1144 @@
+// Persistent batch-1 decode step for Qwen3-0.6B on B200 (sm_100a).
+//
+// One cooperative launch, one CTA per SM, runs a whole decode step: embedding,
+// 28 x [RMSNorm, QKV, QK-norm, RoPE, KV write, GQA attention, O + residual,
+// RMSNorm, gate/up + SiLU*mul, down + residual], final norm, tied LM head and
+// argmax.  Replaces the reference's cooperative kernel + two LM-head kernels
+// (csrc/megakernel/fused_decode_ldg.cu:617-723, :771-887).
+//
+// Structure (B200-first, not the reference's):
+//  * Every CTA owns a fixed slice of every weight matrix (contiguous rows) and
+//    streams it with bulk async copies (cp.async.bulk, TMA engine) into a ring
+//    of shared-memory stages guarded by mbarriers.  A dedicated producer warp
+//    runs ahead through the CTA's whole per-token tile list (all layers, then
+//    the LM head), so HBM keeps streaming while consumers wait on data.
+//  * There is no grid-wide barrier.  Each phase's outputs are published as
+//    64-bit words {tag, fp32 value} with single relaxed stores; consumers poll
+//    exactly the words they need until the tag matches (flag-in-word
+//    handoff), so a handoff costs one store-to-L2 plus one poll.
+//  * RMSNorms are recomputed redundantly by every CTA from the polled vector.
+//  * Attention is split-K flash decoding: 8 kv heads x C position chunks, one
+//    work unit per CTA, each unit serving both q heads of its kv head (every
+//    K/V byte read once).  With C > 1 the last-arriving unit combines the
+//    partial (max, sum, acc) triples.
+//  * The LM head is fused: each CTA takes a slice of vocabulary rows, keeps a
+//    running (value, index) best, publishes it with one 64-bit atomicMax, and
+//    the last CTA to arrive writes the token.
+//  * Every wait is bounded by %globaltimer; on expiry the CTA records an error
+//    in the workspace and all CTAs leave after their in-flight copies land.
+//
+// Numerics follow the reference PyTorch forward on fp32 weights (demo_e2e.py
+// Backend.TORCH): fp32 activations and residual stream, bf16 K/V cache (the
+// current position's K/V are rounded to bf16 before use, demo_e2e.py:298-300),
+// bf16 RoPE tables, fp32 softmax.
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+#include <vector>
+
+#include "megaqwen_b200.h"
+#include "mq_ptx.cuh"
+
+namespace mq {
+
+typedef __nv_bfloat16 bf16;
+
+constexpr int H = MQ_HIDDEN_SIZE;          // 1024
+constexpr int I = MQ_INTERMEDIATE_SIZE;    // 3072
+constexpr int NQ = MQ_NUM_Q_HEADS;         // 16
+constexpr int NKV = MQ_NUM_KV_HEADS;       // 8
+constexpr int D = MQ_HEAD_DIM;             // 128
+constexpr int QS = NQ * D;                 // 2048
+constexpr int KVS = NKV * D;               // 1024
+constexpr int QKV = QS + 2 * KVS;          // 4096
+constexpr int V = MQ_VOCAB_SIZE;           // 151936
+
+constexpr int NCW = 16;                    // consumer warps
+constexpr int NCT = NCW * 32;              // consumer threads
+constexpr int NTHREADS = NCT + 32;         // + one producer warp
+constexpr int STAGE_BYTES = 32768;
+constexpr int NSTAGES = 6;
+constexpr int MAX_CTAS = 256;
+constexpr int CMAX = MAX_CTAS / NKV;       // max position chunks per kv head
+constexpr int PART_STRIDE = 132;           // floats per (unit, head): m, l, pad, pad, acc[128]
+
+constexpr int QKV_TILE = STAGE_BYTES / (H * 2);      // 16 rows
+constexpr int O_TILE = STAGE_BYTES / (QS * 2);       // 8 rows
+constexpr int GU_TILE = STAGE_BYTES / (2 * H * 2);   // 8 gate+up row pairs
+constexpr int DOWN_TILE = STAGE_BYTES / (I * 2);     // 5 rows
+constexpr int LM_TILE = STAGE_BYTES / (H * 2);       // 16 rows
+constexpr int KV_TILE = STAGE_BYTES / (2 * D * 2);   // 64 positions (K and V)
+static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <= NCW && LM_TILE <= NCW,
+              "one consumer warp per row of a tile");
+
+constexpr int BAR_CONSUMERS = 1;           // named barrier id for the consumer warps
+
+// ---- workspace layout (bytes) ------------------------------------------------
+struct Control {
+    uint32_t epoch;               // bumped by the last CTA of every successful step
+    uint32_t error;               // first error code (0 = none)
+    uint32_t info;                // where the first error happened (phase<<8 | layer)
+    uint32_t lm_count;            // arrivals at the LM-head argmax
+    unsigned long long lm_best;   // packed (ordered value, ~index) running max
+    int32_t last_token;
+    int32_t last_position;
+    uint32_t attn_count[NKV];     // arrivals per kv head for split-K combine
+    uint32_t pad[48];
+};
+static_assert(sizeof(Control) == 256, "control block is 256 bytes");
+
+constexpr size_t OFF_CTRL = 0;
+constexpr size_t OFF_QKV = 256;
+constexpr size_t OFF_ATTN = OFF_QKV + 2ull * QKV * 8;
+constexpr size_t OFF_HMID = OFF_ATTN + 2ull * QS * 8;
+constexpr size_t OFF_ACT = OFF_HMID + 2ull * H * 8;
+constexpr size_t OFF_HOUT = OFF_ACT + 2ull * I * 8;
+constexpr size_t OFF_PART = OFF_HOUT + 2ull * H * 8;
+constexpr size_t WS_BYTES = OFF_PART + (size_t)NKV * CMAX * 2 * PART_STRIDE * 4;
+
+// ---- shared memory layout (bytes, dynamic) -------------------------------------
+constexpr int SM_STAGES = 0;
+constexpr int SM_X = SM_STAGES + NSTAGES * STAGE_BYTES;  // fp32 [3072], planar (see store_x)
+constexpr int SM_H2 = SM_X + I * 4;                       // fp32 [1024] post-attention residual
+constexpr int SM_ACC = SM_X;                              // attention combine acc [16][2][128] aliases X,H2
+constexpr int SM_H = SM_H2 + H * 4;                       // fp32 [1024] layer-input residual
+constexpr int SM_QKVRAW = SM_H + H * 4;                   // fp32 [512]  raw q(256) k(128) v(128)
+constexpr int SM_QN = SM_QKVRAW + 512 * 4;                // fp32 [256]  normed+roped q of 2 heads
+constexpr int SM_KP = SM_QN + 256 * 4;                    // fp32 [128]  bf16-rounded k of position p
+constexpr int SM_VP = SM_KP + 128 * 4;                    // fp32 [128]  bf16-rounded v of position p
+constexpr int SM_ML = SM_VP + 128 * 4;                    // fp32 [16][2][2] per-warp (m, l)
+constexpr int SM_RED = SM_ML + NCW * 4 * 4;               // fp32 [2][16]
+constexpr int SM_BEST = SM_RED + 2 * NCW * 4;             // fp32 [16] + int [16]
+constexpr int SM_FLAGS = SM_BEST + 2 * NCW * 4;           // int [4]
+constexpr int SM_BARS = SM_FLAGS + 16;                    // uint64 full[NSTAGES], empty[NSTAGES]
+constexpr int SMEM_BYTES = SM_BARS + 2 * NSTAGES * 8;
+static_assert(SM_ACC + NCW * 2 * D * 4 <= SM_H, "attention combine scratch fits in X+H2");
+static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+static_assert(SM_BARS % 8 == 0, "mbarrier alignment");
+
+enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_LM = 5 };
+
+struct KParams {
+    int input_token;
+    const int* input_token_ptr;
+    int* output_token;
+    float* logits;
+    const bf16* embed;
+    const LDGLayerWeights* layers;
+    const bf16* final_norm;
+    const bf16* lm_head;
+    const bf16* cos_table;
+    const bf16* sin_table;
+    bf16* k_cache;
+    bf16* v_cache;
+    bf16* hidden_out;
+    float* norm_out;
+    uint8_t* ws;
+    int num_layers;
+    int position;
+    int* position_ptr;
+    int max_seq_len;
+    float attn_scale;
+    int attn_chunk;
+    long long timeout_ns;
+    int inject_skip_cta;
+};
+
+// Per-CTA slice of every phase (identical on the producer and consumer side).
+struct Sched {
+    int G, c;
+    int pos, L;                       // position and cache length (pos + 1)
+    int tag_base;                     // (epoch + 1) << 6
+    int qkv_a, qkv_b, o_a, o_b, gu_a, gu_b, dn_a, dn_b, lm_a, lm_b;
+    int has_unit, ug, uj, C, kv_s, kv_e, last;
+};
+
+__device__ __forceinline__ int split_at(int n, int G, int c) { return (int)(((long long)c * n) / G); }
+
+__device__ __forceinline__ uint32_t tag_of(const Sched& S, int layer) { return (uint32_t)S.tag_base | (uint32_t)layer; }
+
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t tag) {
+    return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+}
+
+__device__ __forceinline__ Control* ctrl_of(const KParams& P) { return reinterpret_cast<Control*>(P.ws + OFF_CTRL); }
+__device__ __forceinline__ uint64_t* ll_qkv(const KParams& P, int l) {
+    return reinterpret_cast<uint64_t*>(P.ws + OFF_QKV) + (size_t)(l & 1) * QKV;
+}
+__device__ __forceinline__ uint64_t* ll_attn(const KParams& P, int l) {
+    return reinterpret_cast<uint64_t*>(P.ws + OFF_ATTN) + (size_t)(l & 1) * QS;
+}
+__device__ __forceinline__ uint64_t* ll_hmid(const KParams& P, int l) {
+    return reinterpret_cast<uint64_t*>(P.ws + OFF_HMID) + (size_t)(l & 1) * H;
+}
+__device__ __forceinline__ uint64_t* ll_act(const KParams& P, int l) {
+    return reinterpret_cast<uint64_t*>(P.ws + OFF_ACT) + (size_t)(l & 1) * I;
+}
+__device__ __forceinline__ uint64_t* ll_hout(const KParams& P, int l) {
+    return reinterpret_cast<uint64_t*>(P.ws + OFF_HOUT) + (size_t)(l & 1) * H;
+}
+__device__ __forceinline__ float* part_of(const KParams& P, int g, int j, int h) {
+    return reinterpret_cast<float*>(P.ws + OFF_PART) + ((size_t)(g * CMAX + j) * 2 + h) * PART_STRIDE;
+}
+
+__device__ __forceinline__ void record_error(const KParams& P, uint32_t code, uint32_t info) {
+    Control* C = ctrl_of(P);
+    if (atomicCAS(&C->error, 0u, code) == 0u) atomicExch(&C->info, info);
+}
+
+__device__ __forceinline__ bool global_error(const KParams& P) { return ld_relaxed_u32(&ctrl_of(P)->error) != 0u; }
+
+// Planar storage of an fp32 vector of length K (multiple of 8): element i of
+// 8-group c lives at c*4 + (i&3) in plane (i>>2)&1, planes K/2 floats apart.
+// A lane reading 8-groups l, l+32, ... then issues conflict-free 16-byte loads.
+__device__ __forceinline__ int planar_index(int i, int K) { return ((i >> 2) & 1) * (K >> 1) + (i >> 3) * 4 + (i & 3); }
+
+__device__ __forceinline__ float dot8(uint4 w, float4 lo, float4 hi) {
+    float s = bf16lo(w.x) * lo.x;
+    s = fmaf(bf16hi(w.x), lo.y, s);
+    s = fmaf(bf16lo(w.y), lo.z, s);
+    s = fmaf(bf16hi(w.y), lo.w, s);
+    s = fmaf(bf16lo(w.z), hi.x, s);
+    s = fmaf(bf16hi(w.z), hi.y, s);
+    s = fmaf(bf16lo(w.w), hi.z, s);
+    s = fmaf(bf16hi(w.w), hi.w, s);
+    return s;
+}
+
+// ---- the per-CTA tile walk, shared by producer and consumers --------------------
+template <class Vis>
+__device__ __forceinline__ void walk(const KParams& P, const Sched& S, Vis& v) {
+    for (int l = 0; l < P.num_layers; ++l) {
+        const LDGLayerWeights* W = P.layers + l;
+        const char* wq = (const char*)W->q_proj_weight;
+        const char* wk = (const char*)W->k_proj_weight;
+        const char* wv = (const char*)W->v_proj_weight;
+        const char* wo = (const char*)W->o_proj_weight;
+        const char* wg = (const char*)W->gate_proj_weight;
+        const char* wu = (const char*)W->up_proj_weight;
+        const char* wd = (const char*)W->down_proj_weight;
+
+        if (!v.begin(PH_QKV, l)) return;
+        for (int r = S.qkv_a; r < S.qkv_b;) {
+            const char* base;
+            int r0, lim;
+            if (r < QS) { base = wq; r0 = r; lim = QS; }
+            else if (r < QS + KVS) { base = wk; r0 = r - QS; lim = QS + KVS; }
+            else { base = wv; r0 = r - QS - KVS; lim = QKV; }
+            int n = min(min(S.qkv_b, lim) - r, QKV_TILE);
+            v.tile(PH_QKV, l, r, n, base + (size_t)r0 * H * 2, n * H * 2, nullptr, 0);
+            r += n;
+        }
+        if (S.has_unit) {
+            if (!v.begin(PH_ATTN, l)) return;
+            for (int t = S.kv_s; t < S.kv_e; t += KV_TILE) {
+                int n = min(S.kv_e - t, KV_TILE);
+                size_t off = (((size_t)l * NKV + S.ug) * P.max_seq_len + t) * D * 2;
+                v.tile(PH_ATTN, l, t, n, (const char*)P.k_cache + off, n * D * 2, (const char*)P.v_cache + off,
+                       n * D * 2);
+            }
+            v.end_attn(l);
+        }
+        if (!v.begin(PH_O, l)) return;
+        for (int r = S.o_a; r < S.o_b;) {
+            int n = min(S.o_b - r, O_TILE);
+            v.tile(PH_O, l, r, n, wo + (size_t)r * QS * 2, n * QS * 2, nullptr, 0);
+            r += n;
+        }
+        if (!v.begin(PH_GU, l)) return;
+        for (int r = S.gu_a; r < S.gu_b;) {
+            int n = min(S.gu_b - r, GU_TILE);
+            v.tile(PH_GU, l, r, n, wg + (size_t)r * H * 2, n * H * 2, wu + (size_t)r * H * 2, n * H * 2);
+            r += n;
+        }
+        if (!v.begin(PH_DOWN, l)) return;
+        for (int r = S.dn_a; r < S.dn_b;) {
+            int n = min(S.dn_b - r, DOWN_TILE);
+            v.tile(PH_DOWN, l, r, n, wd + (size_t)r * I * 2, n * I * 2, nullptr, 0);
+            r += n;
+        }
+    }
+    if (!v.begin(PH_LM, P.num_layers)) return;
+    for (int r = S.lm_a; r < S.lm_b;) {
+        int n = min(S.lm_b - r, LM_TILE);
+        v.tile(PH_LM, P.num_layers, r, n, (const char*)P.lm_head + (size_t)r * H * 2, n * H * 2, nullptr, 0);
+        r += n;
+    }
+    v.end_lm();
+}
+
+// ---- producer: one thread issuing bulk copies into the stage ring ---------------
+struct Producer {
+    const KParams& P;
+    uint8_t* smem;
+    uint64_t* full;
+    uint64_t* empty;
+    volatile int* flags;
+    uint32_t n = 0;          // tiles issued
+    bool ok = true;
+    uint64_t policy;
+
+    __device__ Producer(const KParams& p, uint8_t* s) : P(p), smem(s) {
+        full = reinterpret_cast<uint64_t*>(s + SM_BARS);
+        empty = full + NSTAGES;
+        flags = reinterpret_cast<volatile int*>(s + SM_FLAGS);
+        policy = policy_evict_first();
+    }
+    __device__ bool begin(int, int) { return ok; }
+    __device__ void end_attn(int) {}
+    __device__ void end_lm() {}
+
+    __device__ void tile(int phase, int layer, int, int, const char* src1, int b1, const char* src2, int b2) {
+        if (!ok) return;
+        const uint32_t s = n % NSTAGES;
+        if (n >= (uint32_t)NSTAGES) {
+            const uint32_t par = ((n / NSTAGES) & 1u) ^ 1u;
+            uint64_t t0 = 0;
+            uint32_t spins = 0;
+            while (!mbar_try_wait(&empty[s], par)) {
+                if ((++spins & 63u) == 0) {
+                    uint64_t now = globaltimer_ns();
+                    if (t0 == 0) t0 = now;
+                    if (flags[0] != 0 || global_error(P) || (long long)(now - t0) > P.timeout_ns) {
+                        if (flags[0] == 0 && !global_error(P))
+                            record_error(P, MQ_ERR_PIPE_TIMEOUT, 0x100u | ((uint32_t)phase << 8) | layer);
+                        ok = false;
+                        return;
+                    }
+                }
+            }
+        }
+        uint8_t* dst = smem + SM_STAGES + s * STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(b1 + b2));
+        bulk_g2s(dst, src1, (uint32_t)b1, &full[s], policy);
+        if (b2) bulk_g2s(dst + b1, src2, (uint32_t)b2, &full[s], policy);
+        ++n;
+    }
+
+    // Wait (bounded) for every issued copy to land before the CTA may exit.
+    __device__ void drain() {
+        uint32_t first = n > (uint32_t)NSTAGES ? n - NSTAGES : 0;
+        for (uint32_t k = first; k < n; ++k) {
+            const uint32_t s = k % NSTAGES, par = (k / NSTAGES) & 1u;
+            uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[s], par)) {
+                if ((long long)(globaltimer_ns() - t0) > P.timeout_ns) break;
+            }
+        }
+    }
+};
+
+// ---- consumers: 16 warps computing on staged tiles -------------------------------
+struct Consumer {
+    const KParams& P;
+    const Sched& S;
+    uint8_t* smem;
+    uint64_t* full;
+    uint64_t* empty;
+    volatile int* flags;
+    float* sx;
+    float* sh;
+    float* sh2;
+    float* sred;
+    int ct, warp, lane;
+    uint32_t n = 0;          // tiles consumed
+    bool ok = true;          // this thread's view; made collective at begin()
+    int red_par = 0;
+    float xr[32];            // this lane's slice of a K=1024 input vector
+    // attention state: two q heads of one kv head; lane owns dims 4*lane..4*lane+3
+    float q0[4], q1[4], a0[4], a1[4];
+    float m0, l0, m1, l1;
+    // LM-head running best (lane 0 of each warp)
+    float best_v;
+    int best_i;
+
+    __device__ Consumer(const KParams& p, const Sched& s, uint8_t* sm) : P(p), S(s), smem(sm) {
+        full = reinterpret_cast<uint64_t*>(sm + SM_BARS);
+        empty = full + NSTAGES;
+        flags = reinterpret_cast<volatile int*>(sm + SM_FLAGS);
+        sx = reinterpret_cast<float*>(sm + SM_X);
+        sh = reinterpret_cast<float*>(sm + SM_H);
+        sh2 = reinterpret_cast<float*>(sm + SM_H2);
+        sred = reinterpret_cast<float*>(sm + SM_RED);
+        ct = threadIdx.x - 32;
+        warp = ct >> 5;
+        lane = ct & 31;
+        best_v = -INFINITY;
+        best_i = 0x7fffffff;
+    }
+
+    __device__ void fail(uint32_t code, uint32_t info) {
+        if (ok) {
+            if (!global_error(P)) record_error(P, code, info);
+            flags[0] = 1;
+        }
+        ok = false;
+    }
+
+    // Poll n tagged words src[idx] (idx = ct + k*NCT, k < 8) into vals; bounded.
+    __device__ int poll(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info) {
+        int cnt = 0;
+        uint32_t pending = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (ct + k * NCT < count) { pending |= 1u << k; cnt = k + 1; }
+        if (!ok) return cnt;
+        uint64_t t0 = 0;
+        uint32_t spins = 0;
+        while (pending) {
+            uint64_t w[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (pending & (1u << k)) w[k] = ld_relaxed_u64(src + ct + k * NCT);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if ((pending & (1u << k)) && (uint32_t)(w[k] >> 32) == tag) {
+                    vals[k] = __uint_as_float((uint32_t)w[k]);
+                    pending &= ~(1u << k);
+                }
+            if (pending && ((++spins & 31u) == 0)) {
+                uint64_t now = globaltimer_ns();
+                if (t0 == 0) t0 = now;
+                if (flags[0] != 0 || global_error(P)) { ok = false; break; }
+                if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, info); break; }
+            }
+        }
+        return cnt;
+    }
+
+    // Collective: all consumer threads agree on failure.
+    __device__ bool agree() {
+        bool bad = named_bar_or(BAR_CONSUMERS, NCT, !ok);
+        if (bad) ok = false;
+        return !bad;
+    }
+
+    __device__ float block_sum(float v) {
+        // caller guarantees a barrier separates consecutive uses of one parity
+        float* r = sred + red_par * NCW;
+        red_par ^= 1;
+        v = warp_sum(v);
+        if (lane == 0) r[warp] = v;
+        return 0.f;  // the total is read after the next barrier via read_sum()
+    }
+    __device__ float read_sum() {
+        const float* r = sred + (red_par ^ 1) * NCW;
+        float s = 0.f;
+#pragma unroll
+        for (int i = 0; i < NCW; ++i) s += r[i];
+        return s;
+    }
+
+    // Store this thread's normalized K=1024 vector elements into X (planar) and
+    // then load the lane's register slice.  v[k] holds element ct + k*NCT.
+    __device__ void publish_norm_1024(const float* v, float rstd, const bf16* w) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            int i = ct + k * NCT;
+            sx[planar_index(i, H)] = v[k] * rstd * __bfloat162float(w[i]);
+        }
+        named_bar_sync(BAR_CONSUMERS, NCT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            int c = lane + 32 * u;
+            float4 lo = *reinterpret_cast<const float4*>(sx + c * 4);
+            float4 hi = *reinterpret_cast<const float4*>(sx + H / 2 + c * 4);
+            xr[u * 8 + 0] = lo.x; xr[u * 8 + 1] = lo.y; xr[u * 8 + 2] = lo.z; xr[u * 8 + 3] = lo.w;
+            xr[u * 8 + 4] = hi.x; xr[u * 8 + 5] = hi.y; xr[u * 8 + 6] = hi.z; xr[u * 8 + 7] = hi.w;
+        }
+    }
+
+    __device__ bool begin(int phase, int l) {
+        float v[8];
+        if (phase == PH_QKV || phase == PH_LM) {
+            // Layer input h: the embedding row (layer 0) or the previous layer's output.
+            if (l == 0) {
+                const bf16* row = P.embed + (size_t)flags[1] * H;
+                v[0] = __bfloat162float(row[ct]);
+                v[1] = __bfloat162float(row[ct + NCT]);
+            } else {
+                poll(ll_hout(P, l - 1), H, tag_of(S, l - 1), v, ((uint32_t)phase << 8) | l);
+            }
+            if (ok) {
+                sh[ct] = v[0];
+                sh[ct + NCT] = v[1];
+            }
+            block_sum(v[0] * v[0] + v[1] * v[1]);
+            if (!agree()) return false;
+            float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
+            const bf16* w = (phase == PH_LM) ? P.final_norm : (const bf16*)P.layers[l].input_layernorm_weight;
+            if (phase == PH_LM && S.c == 0) {
+                if (P.hidden_out) {
+                    P.hidden_out[ct] = __float2bfloat16(v[0]);
+                    P.hidden_out[ct + NCT] = __float2bfloat16(v[1]);
+                }
+                if (P.norm_out) {
+                    P.norm_out[ct] = v[0] * rstd * __bfloat162float(w[ct]);
+                    P.norm_out[ct + NCT] = v[1] * rstd * __bfloat162float(w[ct + NCT]);
+                }
+            }
+            publish_norm_1024(v, rstd, w);
+            return true;
+        }
+        if (phase == PH_GU) {
+            poll(ll_hmid(P, l), H, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
+            if (ok) {
+                sh2[ct] = v[0];
+                sh2[ct + NCT] = v[1];
+            }
+            block_sum(v[0] * v[0] + v[1] * v[1]);
+            if (!agree()) return false;
+            float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
+            publish_norm_1024(v, rstd, (const bf16*)P.layers[l].post_attn_layernorm_weight);
+            return true;
+        }
+        if (phase == PH_O || phase == PH_DOWN) {
+            const int K = (phase == PH_O) ? QS : I;
+            const uint64_t* src = (phase == PH_O) ? ll_attn(P, l) : ll_act(P, l);
+            int cnt = poll(src, K, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
+            if (!agree()) return false;
+            for (int k = 0; k < cnt; ++k) {
+                int i = ct + k * NCT;
+                if (i < K) sx[planar_index(i, K)] = v[k];
+            }
+            named_bar_sync(BAR_CONSUMERS, NCT);
+            return true;
+        }
+        // PH_ATTN: raw q (2 heads), k, v of kv head g -> smem, then QK-norm + RoPE.
+        {
+            const int g = S.ug;
+            const uint64_t* src = ll_qkv(P, l);
+            float* raw = reinterpret_cast<float*>(smem + SM_QKVRAW);
+            // 512 words: q rows [256g, 256g+256), k rows [2048+128g, +128), v rows [3072+128g, +128)
+            int idx = ct < 256 ? 256 * g + ct : (ct < 384 ? QS + 128 * g + (ct - 256) : QS + KVS + 128 * g + (ct - 384));
+            float val = 0.f;
+            if (ok) {
+                uint64_t t0 = 0;
+                uint32_t spins = 0;
+                const uint32_t tag = tag_of(S, l);
+                while (true) {
+                    uint64_t w = ld_relaxed_u64(src + idx);
+                    if ((uint32_t)(w >> 32) == tag) { val = __uint_as_float((uint32_t)w); break; }
+                    if ((++spins & 31u) == 0) {
+                        uint64_t now = globaltimer_ns();
+                        if (t0 == 0) t0 = now;
+                        if (flags[0] != 0 || global_error(P)) { ok = false; break; }
+                        if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, (1u << 8) | l); break; }
+                    }
+                }
+            }
+            if (!agree()) return false;
+            raw[ct] = val;
+            named_bar_sync(BAR_CONSUMERS, NCT);
+            float* qn = reinterpret_cast<float*>(smem + SM_QN);
+            float* kp = reinterpret_cast<float*>(smem + SM_KP);
+            float* vp = reinterpret_cast<float*>(smem + SM_VP);
+            const LDGLayerWeights* W = P.layers + l;
+            if (warp < 3) {
+                // warps 0,1: q heads 2g, 2g+1; warp 2: k head g.  Lane owns elements
+                // lane + 32m (m = 0..3); rotate-half pairs (m, m+2) stay in the lane.
+                const float* x = raw + (warp < 2 ? warp * D : 256);
+                const bf16* nw = (const bf16*)(warp < 2 ? W->q_norm_weight : W->k_norm_weight);
+                float e[4];
+                float ss = 0.f;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) { e[m] = x[lane + 32 * m]; ss += e[m] * e[m]; }
+                ss = warp_sum(ss);
+                float r = rsqrtf(ss / (float)D + 1e-6f);
+#pragma unroll
+                for (int m = 0; m < 4; ++m) e[m] = e[m] * r * __bfloat162float(nw[lane + 32 * m]);
+                const bf16* cs = P.cos_table + (size_t)S.pos * D;
+                const bf16* sn = P.sin_table + (size_t)S.pos * D;
+                float o[4];
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    int i = lane + 32 * m;
+                    float c = __bfloat162float(cs[i]), s = __bfloat162float(sn[i]);
+                    o[m] = (m < 2) ? (e[m] * c - e[m + 2] * s) : (e[m] * c + e[m - 2] * s);
+                }
+                if (warp < 2) {
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) qn[warp * D + lane + 32 * m] = o[m];
+                } else {
+                    bf16* kc = P.k_cache + (((size_t)l * NKV + g) * P.max_seq_len + S.pos) * D;
+#pragma unroll
+                    for (int m = 0; m < 4; ++m) {
+                        bf16 b = __float2bfloat16(o[m]);
+                        kp[lane + 32 * m] = __bfloat162float(b);
+                        if (S.last) kc[lane + 32 * m] = b;
+                    }
+                }
+            } else if (warp == 3) {
+                const float* x = raw + 384;
+                bf16* vc = P.v_cache + (((size_t)l * NKV + g) * P.max_seq_len + S.pos) * D;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    bf16 b = __float2bfloat16(x[lane + 32 * m]);
+                    vp[lane + 32 * m] = __bfloat162float(b);
+                    if (S.last) vc[lane + 32 * m] = b;
+                }
+            }
+            named_bar_sync(BAR_CONSUMERS, NCT);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                q0[i] = qn[4 * lane + i] * P.attn_scale;
+                q1[i] = qn[D + 4 * lane + i] * P.attn_scale;
+                a0[i] = 0.f;
+                a1[i] = 0.f;
+            }
+            m0 = m1 = -INFINITY;
+            l0 = l1 = 0.f;
+            return true;
+        }
+    }
+
+    // Warp-uniform bounded wait for stage s to fill (all lanes iterate together).
+    __device__ bool wait_full(uint32_t s, uint32_t par, int phase, int l) {
+        if (!ok) return false;
+        uint64_t t0 = 0;
+        uint32_t spins = 0;
+        while (!__all_sync(0xffffffffu, mbar_try_wait(&full[s], par))) {
+            if ((++spins & 63u) == 0) {
+                int verdict = 0;
+                if (lane == 0) {
+                    uint64_t now = globaltimer_ns();
+                    if (t0 == 0) t0 = now;
+                    if (flags[0] != 0 || global_error(P)) verdict = 1;
+                    else if ((long long)(now - t0) > P.timeout_ns) verdict = 2;
+                }
+                verdict = __shfl_sync(0xffffffffu, verdict, 0);
+                if (verdict == 1) { ok = false; return false; }
+                if (verdict == 2) {
+                    if (lane == 0) fail(MQ_ERR_PIPE_TIMEOUT, 0x200u | ((uint32_t)phase << 8) | l);
+                    ok = false;
+                    return false;
+                }
+            }
+        }
+        return true;
+    }
+
+    __device__ __forceinline__ void attn_pos(const uint2 kq, const uint2 vq) {
+        float k0 = bf16lo(kq.x), k1 = bf16hi(kq.x), k2 = bf16lo(kq.y), k3 = bf16hi(kq.y);
+        float s0 = q0[0] * k0 + q0[1] * k1 + q0[2] * k2 + q0[3] * k3;
+        float s1 = q1[0] * k0 + q1[1] * k1 + q1[2] * k2 + q1[3] * k3;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        }
+        float v0 = bf16lo(vq.x), v1 = bf16hi(vq.x), v2 = bf16lo(vq.y), v3 = bf16hi(vq.y);
+        float n0 = fmaxf(m0, s0), c0 = expf(m0 - n0), p0 = expf(s0 - n0);
+        float n1 = fmaxf(m1, s1), c1 = expf(m1 - n1), p1 = expf(s1 - n1);
+        l0 = l0 * c0 + p0;
+        l1 = l1 * c1 + p1;
+        a0[0] = a0[0] * c0 + p0 * v0; a0[1] = a0[1] * c0 + p0 * v1; a0[2] = a0[2] * c0 + p0 * v2; a0[3] = a0[3] * c0 + p0 * v3;
+        a1[0] = a1[0] * c1 + p1 * v0; a1[1] = a1[1] * c1 + p1 * v1; a1[2] = a1[2] * c1 + p1 * v2; a1[3] = a1[3] * c1 + p1 * v3;
+        m0 = n0;
+        m1 = n1;
+    }
+
+    __device__ void tile(int phase, int l, int r0, int nrows, const char*, int b1, const char*, int) {
+        const uint32_t s = n % NSTAGES, par = (n / NSTAGES) & 1u;
+        ++n;
+        if (!wait_full(s, par, phase, l)) return;
+        const uint8_t* st = smem + SM_STAGES + s * STAGE_BYTES;
+        const uint32_t tag = tag_of(S, l);
+        if (phase == PH_ATTN) {
+            const uint8_t* kb = st;
+            const uint8_t* vb = st + b1;
+            for (int t = warp; t < nrows; t += NCW) {
+                uint2 kq = *reinterpret_cast<const uint2*>(kb + t * D * 2 + lane * 8);
+                uint2 vq = *reinterpret_cast<const uint2*>(vb + t * D * 2 + lane * 8);
+                attn_pos(kq, vq);
+            }
+        } else if (warp < nrows) {
+            const int r = r0 + warp;
+            if (phase == PH_QKV || phase == PH_LM || phase == PH_GU) {
+                const uint4* w = reinterpret_cast<const uint4*>(st + warp * H * 2);
+                float acc = 0.f;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    uint4 q = w[lane + 32 * u];
+                    const float* x = xr + 8 * u;
+                    acc += dot8(q, make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]));
+                }
+                if (phase == PH_GU) {
+                    const uint4* wu = reinterpret_cast<const uint4*>(st + b1 + warp * H * 2);
+                    float up = 0.f;
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        uint4 q = wu[lane + 32 * u];
+                        const float* x = xr + 8 * u;
+                        up += dot8(q, make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]));
+                    }
+                    acc = warp_sum(acc);
+                    up = warp_sum(up);
+                    if (lane == 0) {
+                        float act = acc / (1.0f + expf(-acc)) * up;
+                        st_relaxed_u64(ll_act(P, l) + r, ll_word(act, tag));
+                    }
+                } else {
+                    acc = warp_sum(acc);
+                    if (phase == PH_QKV) {
+                        bool skip = (S.c == P.inject_skip_cta - 1) && l == 0;
+                        if (lane == 0 && !skip) st_relaxed_u64(ll_qkv(P, l) + r, ll_word(acc, tag));
+                    } else {
+                        if (lane == 0) {
+                            if (P.logits) P.logits[r] = acc;
+                            if (acc > best_v || (acc == best_v && r < best_i)) { best_v = acc; best_i = r; }
+                        }
+                    }
+                }
+            } else {
+                // O (K=2048) and down (K=3072): x from planar shared memory.
+                const int K = (phase == PH_O) ? QS : I;
+                const int CPL = K / 256;  // 16-byte chunks per lane
+                const uint4* w = reinterpret_cast<const uint4*>(st + warp * K * 2);
+                float acc = 0.f;
+#pragma unroll 4
+                for (int u = 0; u < CPL; ++u) {
+                    int c = lane + 32 * u;
+                    float4 lo = *reinterpret_cast<const float4*>(sx + c * 4);
+                    float4 hi = *reinterpret_cast<const float4*>(sx + K / 2 + c * 4);
+                    acc += dot8(w[c], lo, hi);
+                }
+                acc = warp_sum(acc);
+                if (lane == 0) {
+                    if (phase == PH_O) st_relaxed_u64(ll_hmid(P, l) + r, ll_word(acc + sh[r], tag));
+                    else st_relaxed_u64(ll_hout(P, l) + r, ll_word(acc + sh2[r], tag));
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    __device__ void end_attn(int l) {
+        float* acc = reinterpret_cast<float*>(smem + SM_ACC);   // [16][2][128]
+        float* ml = reinterpret_cast<float*>(smem + SM_ML);     // [16][2][2]
+        if (ok && S.last && warp == 0) {
+            // the current position, from the bf16-rounded values in shared memory
+            const float* kp = reinterpret_cast<const float*>(smem + SM_KP);
+            const float* vp = reinterpret_cast<const float*>(smem + SM_VP);
+            float k0 = kp[4 * lane], k1 = kp[4 * lane + 1], k2 = kp[4 * lane + 2], k3 = kp[4 * lane + 3];
+            float s0 = q0[0] * k0 + q0[1] * k1 + q0[2] * k2 + q0[3] * k3;
+            float s1 = q1[0] * k0 + q1[1] * k1 + q1[2] * k2 + q1[3] * k3;
+            s0 = warp_sum(s0);
+            s1 = warp_sum(s1);
+            float n0 = fmaxf(m0, s0), c0 = expf(m0 - n0), p0 = expf(s0 - n0);
+            float n1 = fmaxf(m1, s1), c1 = expf(m1 - n1), p1 = expf(s1 - n1);
+            l0 = l0 * c0 + p0;
+            l1 = l1 * c1 + p1;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float vv = vp[4 * lane + i];
+                a0[i] = a0[i] * c0 + p0 * vv;
+                a1[i] = a1[i] * c1 + p1 * vv;
+            }
+            m0 = n0;
+            m1 = n1;
+        }
+        if (lane == 0) {
+            ml[warp * 4 + 0] = m0; ml[warp * 4 + 1] = l0;
+            ml[warp * 4 + 2] = m1; ml[warp * 4 + 3] = l1;
+        }
+        *reinterpret_cast<float4*>(acc + (warp * 2 + 0) * D + 4 * lane) = make_float4(a0[0], a0[1], a0[2], a0[3]);
+        *reinterpret_cast<float4*>(acc + (warp * 2 + 1) * D + 4 * lane) = make_float4(a1[0], a1[1], a1[2], a1[3]);
+        named_bar_sync(BAR_CONSUMERS, NCT);
+        float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
+        const int h = warp;  // warps 0 and 1 combine heads 0 and 1
+        if (warp < 2) {
+            for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[w * 4 + 2 * h]);
+            for (int w = 0; w < NCW; ++w) {
+                float e = expf(ml[w * 4 + 2 * h] - M);
+                Ls += ml[w * 4 + 2 * h + 1] * e;
+                float4 a = *reinterpret_cast<const float4*>(acc + (w * 2 + h) * D + 4 * lane);
+                A[0] += a.x * e; A[1] += a.y * e; A[2] += a.z * e; A[3] += a.w * e;
+            }
+        }
+        const uint32_t tag = tag_of(S, l);
+        uint64_t* out = ll_attn(P, l) + 256 * S.ug;
+        if (S.C == 1) {
+            if (warp < 2 && ok) {
+                float inv = 1.0f / Ls;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) st_relaxed_u64(out + h * D + 4 * lane + i, ll_word(A[i] * inv, tag));
+            }
+            return;
+        }
+        // split-K: publish the partial, the last unit of this kv head combines
+        volatile int* f = flags;
+        if (warp < 2) {
+            float* pp = part_of(P, S.ug, S.uj, h);
+            if (lane == 0) { pp[0] = M; pp[1] = Ls; }
+            *reinterpret_cast<float4*>(pp + 4 + 4 * lane) = make_float4(A[0], A[1], A[2], A[3]);
+            __threadfence();
+        }
+        named_bar_sync(BAR_CONSUMERS, NCT);
+        if (ct == 0) {
+            Control* C = ctrl_of(P);
+            uint32_t old = atomicAdd(&C->attn_count[S.ug], 1u);
+            int last = (old == (uint32_t)(S.C - 1));
+            if (last) {
+                atomicExch(&C->attn_count[S.ug], 0u);
+                __threadfence();
+            }
+            f[2] = last;
+        }
+        named_bar_sync(BAR_CONSUMERS, NCT);
+        if (f[2] && warp < 2 && ok) {
+            float gm = -INFINITY;
+            for (int j = 0; j < S.C; ++j) gm = fmaxf(gm, ld_relaxed_f32(part_of(P, S.ug, j, h)));
+            float gl = 0.f, G4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int j = 0; j < S.C; ++j) {
+                const float* pp = part_of(P, S.ug, j, h);
+                float e = expf(ld_relaxed_f32(pp) - gm);
+                gl += ld_relaxed_f32(pp + 1) * e;
+                float4 a = __ldcg(reinterpret_cast<const float4*>(pp + 4 + 4 * lane));
+                G4[0] += a.x * e; G4[1] += a.y * e; G4[2] += a.z * e; G4[3] += a.w * e;
+            }
+            float inv = 1.0f / gl;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) st_relaxed_u64(out + h * D + 4 * lane + i, ll_word(G4[i] * inv, tag));
+        }
+    }
+
+    __device__ void end_lm() {
+        float* bv = reinterpret_cast<float*>(smem + SM_BEST);
+        int* bi = reinterpret_cast<int*>(smem + SM_BEST) + NCW;
+        if (lane == 0) { bv[warp] = best_v; bi[warp] = best_i; }
+        if (!agree()) return;
+        if (ct == 0) {
+            float v = bv[0];
+            int i = bi[0];
+            for (int w = 1; w < NCW; ++w)
+                if (bv[w] > v || (bv[w] == v && bi[w] < i)) { v = bv[w]; i = bi[w]; }
+            uint32_t u = __float_as_uint(v);
+            uint32_t ord = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+            unsigned long long key = ((unsigned long long)ord << 32) | (unsigned long long)(0xffffffffu - (uint32_t)i);
+            Control* C = ctrl_of(P);
+            atomicMax(&C->lm_best, key);
+            __threadfence();
+            uint32_t old = atomicAdd(&C->lm_count, 1u);
+            if (old == (uint32_t)(S.G - 1)) {
+                __threadfence();
+                unsigned long long best = atomicExch(&C->lm_best, 0ull);
+                int tok = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
+                atomicExch(&C->lm_count, 0u);
+                if (P.output_token) *P.output_token = tok;
+                C->last_token = tok;
+                C->last_position = S.pos;
+                if (P.position_ptr) *P.position_ptr = S.pos + 1;
+                C->epoch = (C->epoch + 1u) & ((1u << 25) - 1u);
+                __threadfence();
+            }
+        }
+    }
+};
+
+__global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_constant__ KParams P) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    Control* C = ctrl_of(P);
+    volatile int* flags = reinterpret_cast<volatile int*>(smem + SM_FLAGS);
+
+    Sched S;
+    S.G = gridDim.x;
+    S.c = blockIdx.x;
+    const int pos = P.position_ptr ? *P.position_ptr : P.position;
+    const int tok = P.input_token_ptr ? *P.input_token_ptr : P.input_token;
+    if (pos < 0 || pos >= P.max_seq_len) {
+        if (S.c == 0 && threadIdx.x == 0) record_error(P, MQ_ERR_BAD_POSITION, (uint32_t)pos);
+        return;
+    }
+    if (tok < 0 || tok >= V) {
+        if (S.c == 0 && threadIdx.x == 0) record_error(P, MQ_ERR_BAD_TOKEN, (uint32_t)tok);
+        return;
+    }
+    S.pos = pos;
+    S.L = pos + 1;
+    S.tag_base = (int)((C->epoch + 1u) << 6);
+    S.qkv_a = split_at(QKV, S.G, S.c); S.qkv_b = split_at(QKV, S.G, S.c + 1);
+    S.o_a = split_at(H, S.G, S.c);     S.o_b = split_at(H, S.G, S.c + 1);
+    S.gu_a = split_at(I, S.G, S.c);    S.gu_b = split_at(I, S.G, S.c + 1);
+    S.dn_a = S.o_a;                    S.dn_b = S.o_b;
+    S.lm_a = split_at(V, S.G, S.c);    S.lm_b = split_at(V, S.G, S.c + 1);
+    {
+        const int chunk = P.attn_chunk > 0 ? P.attn_chunk : 64;
+        int C_ = (S.L + chunk - 1) / chunk;
+        C_ = min(C_, S.G / NKV);
+        C_ = min(C_, CMAX);
+        C_ = max(C_, 1);
+        S.C = C_;
+        const int U = NKV * C_;
+        const int u = (int)(((long long)S.c * U + S.G - 1) / S.G);
+        S.has_unit = (u < U) && (int)(((long long)u * S.G) / U) == S.c;
+        S.ug = u / C_;
+        S.uj = u % C_;
+        const int ps = split_at(S.L, C_, S.uj), pe = split_at(S.L, C_, S.uj + 1);
+        S.last = (S.uj == C_ - 1);
+        S.kv_s = ps;
+        S.kv_e = S.last ? pe - 1 : pe;   // the current position comes from registers, not the cache
+    }
+
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM_BARS);
+    uint64_t* empty = full + NSTAGES;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NSTAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], NCW);
+        }
+        fence_mbar_init();
+        flags[0] = 0;
+        flags[1] = tok;
+        flags[2] = 0;
+    }
+    __syncthreads();
+
+    if (threadIdx.x < 32) {
+        if (threadIdx.x == 0) {
+            Producer pr(P, smem);
+            walk(P, S, pr);
+            pr.drain();
+        }
+        return;
+    }
+    Consumer cs(P, S, smem);
+    walk(P, S, cs);
+}
+
+}  // namespace mq
+
+// =============================================================================
+// Host side: C ABI
+// =============================================================================
+
+namespace {
+
+thread_local int g_last_error = MQ_OK;
+
+struct DeviceWorkspace {
+    void* ptr = nullptr;
+};
+std::mutex g_ws_mutex;
+std::vector<DeviceWorkspace> g_ws;  // one default workspace per device
+
+int set_err(int e) {
+    g_last_error = e;
+    return e;
+}
+
+bool kernel_configured[64] = {false};
+
+int configure_kernel(int dev) {
+    if (dev >= 0 && dev < 64 && kernel_configured[dev]) return MQ_OK;
+    cudaError_t e = cudaFuncSetAttribute(mq::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         mq::SMEM_BYTES);
+    if (e != cudaSuccess) return MQ_ERR_CUDA;
+    if (dev >= 0 && dev < 64) kernel_configured[dev] = true;
+    return MQ_OK;
+}
+
+int default_ctas(int dev) {
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+    int n = sms < mq::MAX_CTAS ? sms : mq::MAX_CTAS;
+    return n;
+}
+
+void* default_workspace(int dev, cudaStream_t stream) {
+    std::lock_guard<std::mutex> lk(g_ws_mutex);
+    if ((int)g_ws.size() <= dev) g_ws.resize(dev + 1);
+    if (!g_ws[dev].ptr) {
+        void* p = nullptr;
+        if (cudaMalloc(&p, mq::WS_BYTES) != cudaSuccess) return nullptr;
+        if (cudaMemsetAsync(p, 0, mq::WS_BYTES, stream) != cudaSuccess) return nullptr;
+        g_ws[dev].ptr = p;
+    }
+    return g_ws[dev].ptr;
+}
+
+int launch(const mq_decode_params* p, cudaStream_t stream) {
+    if (!p || !p->embed || !p->layers || !p->final_norm || !p->lm_head || !p->cos_table || !p->sin_table ||
+        !p->k_cache || !p->v_cache)
+        return MQ_ERR_INVALID_ARGUMENT;
+    if (!p->workspace || p->workspace_bytes < mq::WS_BYTES) return MQ_ERR_WORKSPACE;
+    if (p->num_layers < 1 || p->num_layers > MQ_MAX_LAYERS || p->max_seq_len < 1) return MQ_ERR_INVALID_ARGUMENT;
+    if (!p->position_ptr && (p->position < 0 || p->position >= p->max_seq_len)) return MQ_ERR_INVALID_ARGUMENT;
+    if (!p->input_token_ptr && (p->input_token < 0 || p->input_token >= MQ_VOCAB_SIZE))
+        return MQ_ERR_INVALID_ARGUMENT;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MQ_ERR_CUDA;
+    int rc = configure_kernel(dev);
+    if (rc) return rc;
+    int G = p->num_ctas > 0 ? p->num_ctas : default_ctas(dev);
+    if (G < mq::NKV || G > mq::MAX_CTAS) return MQ_ERR_INVALID_ARGUMENT;
+    int maxb = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel, mq::NTHREADS, mq::SMEM_BYTES) !=
+            cudaSuccess || maxb < 1)
+        return MQ_ERR_CUDA;
+    mq::KParams k;
+    k.input_token = p->input_token;
+    k.input_token_ptr = p->input_token_ptr;
+    k.output_token = p->output_token;
+    k.logits = p->logits;
+    k.embed = (const mq::bf16*)p->embed;
+    k.layers = p->layers;
+    k.final_norm = (const mq::bf16*)p->final_norm;
+    k.lm_head = (const mq::bf16*)p->lm_head;
+    k.cos_table = (const mq::bf16*)p->cos_table;
+    k.sin_table = (const mq::bf16*)p->sin_table;
+    k.k_cache = (mq::bf16*)p->k_cache;
+    k.v_cache = (mq::bf16*)p->v_cache;
+    k.hidden_out = (mq::bf16*)p->hidden_out;
+    k.norm_out = p->normalized_out;
+    k.ws = (uint8_t*)p->workspace;
+    k.num_layers = p->num_layers;
+    k.position = p->position;
+    k.position_ptr = p->position_ptr;
+    k.max_seq_len = p->max_seq_len;
+    k.attn_scale = p->attn_scale;
+    k.attn_chunk = p->attn_chunk;
+    k.timeout_ns = p->timeout_ns > 0 ? p->timeout_ns : 2000000000ll;
+    k.inject_skip_cta = p->inject_skip_cta;
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(mq::NTHREADS);
+    cfg.dynamicSmemBytes = mq::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, mq::decode_step_kernel, k);
+    if (e != cudaSuccess) return MQ_ERR_CUDA;
+    return MQ_OK;
+}
+
+void launch_ref_abi(int input_token_id, int* output_token_id, float* logits, const void* embed_weight,
+                    const LDGLayerWeights* layer_weights, const void* final_norm_weight, const void* lm_head_weight,
+                    const void* cos_table, const void* sin_table, void* k_cache, void* v_cache, void* hidden_buffer,
+                    void* g_normalized, int num_layers, int position, int cache_len, int max_seq_len, float attn_scale,
+                    cudaStream_t stream) {
+    if (cache_len != position + 1) { set_err(MQ_ERR_INVALID_ARGUMENT); return; }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { set_err(MQ_ERR_CUDA); return; }
+    void* ws = default_workspace(dev, stream);
+    if (!ws) { set_err(MQ_ERR_CUDA); return; }
+    mq_decode_params p = {};
+    p.input_token = input_token_id;
+    p.output_token = output_token_id;
+    p.logits = logits;
+    p.embed = embed_weight;
+    p.layers = layer_weights;
+    p.final_norm = final_norm_weight;
+    p.lm_head = lm_head_weight;
+    p.cos_table = cos_table;
+    p.sin_table = sin_table;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.hidden_out = hidden_buffer;
+    p.normalized_out = (float*)g_normalized;
+    p.workspace = ws;
+    p.workspace_bytes = mq::WS_BYTES;
+    p.num_layers = num_layers;
+    p.position = position;
+    p.max_seq_len = max_seq_len;
+    p.attn_scale = attn_scale;
+    set_err(launch(&p, stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+void launch_ldg_decode(int input_token_id, int* output_token_id, const void* embed_weight,
+                       const LDGLayerWeights* layer_weights, const void* final_norm_weight,
+                       const void* lm_head_weight, const void* cos_table, const void* sin_table, void* k_cache,
+                       void* v_cache, void* hidden_buffer, void* /*g_activations*/, void* /*g_residual*/,
+                       void* /*g_q*/, void* /*g_k*/, void* /*g_v*/, void* /*g_attn_out*/,
+                       void* /*g_mlp_intermediate*/, void* g_normalized, void* /*block_max_vals*/,
+                       void* /*block_max_idxs*/, int num_layers, int position, int cache_len, int max_seq_len,
+                       float attn_scale, cudaStream_t stream) {
+    launch_ref_abi(input_token_id, output_token_id, nullptr, embed_weight, layer_weights, final_norm_weight,
+                   lm_head_weight, cos_table, sin_table, k_cache, v_cache, hidden_buffer, g_normalized, num_layers,
+                   position, cache_len, max_seq_len, attn_scale, stream);
+}
+
+void launch_ldg_decode_with_logits(int input_token_id, int* output_token_id, float* logits_output,
+                                   const void* embed_weight, const LDGLayerWeights* layer_weights,
+                                   const void* final_norm_weight, const void* lm_head_weight, const void* cos_table,
+                                   const void* sin_table, void* k_cache, void* v_cache, void* hidden_buffer,
+                                   void* /*g_activations*/, void* /*g_residual*/, void* /*g_q*/, void* /*g_k*/,
+                                   void* /*g_v*/, void* /*g_attn_out*/, void* /*g_mlp_intermediate*/,
+                                   void* g_normalized, void* /*block_max_vals*/, void* /*block_max_idxs*/,
+                                   int num_layers, int position, int cache_len, int max_seq_len, float attn_scale,
+                                   cudaStream_t stream) {
+    launch_ref_abi(input_token_id, output_token_id, logits_output, embed_weight, layer_weights, final_norm_weight,
+                   lm_head_weight, cos_table, sin_table, k_cache, v_cache, hidden_buffer, g_normalized, num_layers,
+                   position, cache_len, max_seq_len, attn_scale, stream);
+}
+
+size_t mq_decode_workspace_bytes(void) { return mq::WS_BYTES; }
+
+int mq_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream) {
+    if (!workspace || bytes < mq::WS_BYTES) return MQ_ERR_WORKSPACE;
+    return cudaMemsetAsync(workspace, 0, mq::WS_BYTES, stream) == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+}
+
+int mq_decode(const mq_decode_params* params, cudaStream_t stream) { return launch(params, stream); }
+
+int mq_decode_read_error(const void* workspace, uint32_t* error, uint32_t* info, cudaStream_t stream) {
+    if (!workspace) return MQ_ERR_WORKSPACE;
+    uint32_t h[3] = {0, 0, 0};
+    if (cudaMemcpyAsync(h, workspace, sizeof(h), cudaMemcpyDeviceToHost, stream) != cudaSuccess) return MQ_ERR_CUDA;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return MQ_ERR_CUDA;
+    if (error) *error = h[1];
+    if (info) *info = h[2];
+    return MQ_OK;
+}
+
+int mq_decode_fetch(const void* workspace, int* token, uint32_t* error, uint32_t* info, cudaStream_t stream) {
+    if (!workspace) return MQ_ERR_WORKSPACE;
+    static thread_local uint32_t* pinned = nullptr;
+    if (!pinned && cudaHostAlloc((void**)&pinned, 64, cudaHostAllocDefault) != cudaSuccess) return MQ_ERR_CUDA;
+    if (cudaMemcpyAsync(pinned, workspace, 32, cudaMemcpyDeviceToHost, stream) != cudaSuccess) return MQ_ERR_CUDA;
+    if (cudaStreamSynchronize(stream) != cudaSuccess) return MQ_ERR_CUDA;
+    const mq::Control* c = reinterpret_cast<const mq::Control*>(pinned);
+    if (token) *token = c->last_token;
+    if (error) *error = c->error;
+    if (info) *info = c->info;
+    return MQ_OK;
+}
+
+int mq_decode_default_ctas(void) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+    return default_ctas(dev);
+}
+
+int mq_get_last_error(void) { return g_last_error; }
+
+const char* mq_error_string(int code) {
+    switch (code) {
+        case MQ_OK: return "ok";
+        case MQ_ERR_INVALID_ARGUMENT: return "invalid argument";
+        case MQ_ERR_WAIT_TIMEOUT: return "inter-CTA handoff wait timed out";
+        case MQ_ERR_PIPE_TIMEOUT: return "shared-memory pipeline wait timed out";
+        case MQ_ERR_BAD_TOKEN: return "input token out of range";
+        case MQ_ERR_BAD_POSITION: return "position out of range";
+        case MQ_ERR_CUDA: return "CUDA runtime error";
+        case MQ_ERR_WORKSPACE: return "workspace missing or too small";
+        default: return "unknown error";
+    }
+}
+
+const char* mq_version(void) { return "megaqwen_b200 0.1"; }
+
+}  // extern "C"

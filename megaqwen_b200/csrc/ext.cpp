@@ -1,0 +1,501 @@
+// Torch extension: the reference's Python-facing classes and module functions,
+// implemented over the C ABI in include/megaqwen_b200.h.
+//
+// Mirrors, by name, arguments and error behaviour:
+//   MegakernelDecoder             csrc/megakernel/megakernel_decode.py:90-242
+//   MegakernelPrefillDecoder      csrc/megakernel/megakernel_decode.py:375-660
+//   MegakernelFusedPrefillDecoder csrc/megakernel/megakernel_decode.py:788-1053
+//   init_ldg_layer_weights / init_ldg_embed_weight / decode_ldg /
+//   decode_ldg_with_logits        chat.py:147-323
+// Differences, all additive: decode steps and prefill check position <
+// max_seq_len and raise RuntimeError; device-side wait failures raise
+// RuntimeError with the engine's error text.
+
+#include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/cuda/CUDAStream.h>
+
+#include <cmath>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "megaqwen_b200.h"
+
+namespace {
+
+constexpr int kHidden = MQ_HIDDEN_SIZE;
+constexpr int kInter = MQ_INTERMEDIATE_SIZE;
+constexpr int kQ = MQ_NUM_Q_HEADS * MQ_HEAD_DIM;
+constexpr int kKV = MQ_NUM_KV_HEADS * MQ_HEAD_DIM;
+constexpr int kVocab = MQ_VOCAB_SIZE;
+
+void check_bf16(const torch::Tensor& t, const char* name, std::vector<int64_t> shape) {
+    if (!t.is_cuda()) throw std::runtime_error(std::string(name) + " must be a CUDA tensor");
+    if (t.scalar_type() != torch::kBFloat16) throw std::runtime_error(std::string(name) + " must be bfloat16");
+    if (!t.is_contiguous()) throw std::runtime_error(std::string(name) + " must be contiguous");
+    if (t.sizes().vec() != shape) throw std::runtime_error(std::string(name) + " has the wrong shape");
+}
+
+std::vector<int64_t> layer_shape(int k) {
+    switch (k) {
+        case 0: return {kHidden};
+        case 1: return {kQ, kHidden};
+        case 2: return {kKV, kHidden};
+        case 3: return {kKV, kHidden};
+        case 4: return {MQ_HEAD_DIM};
+        case 5: return {MQ_HEAD_DIM};
+        case 6: return {kHidden, kQ};
+        case 7: return {kHidden};
+        case 8: return {kInter, kHidden};
+        case 9: return {kInter, kHidden};
+        default: return {kHidden, kInter};
+    }
+}
+
+const char* kLayerNames[11] = {"input_layernorm", "q_proj", "k_proj", "v_proj", "q_norm", "k_norm",
+                               "o_proj", "post_attention_layernorm", "gate_proj", "up_proj", "down_proj"};
+
+LDGLayerWeights make_layer(const std::vector<torch::Tensor>& t, size_t base) {
+    LDGLayerWeights w;
+    w.input_layernorm_weight = t[base + 0].data_ptr();
+    w.q_proj_weight = t[base + 1].data_ptr();
+    w.k_proj_weight = t[base + 2].data_ptr();
+    w.v_proj_weight = t[base + 3].data_ptr();
+    w.q_norm_weight = t[base + 4].data_ptr();
+    w.k_norm_weight = t[base + 5].data_ptr();
+    w.o_proj_weight = t[base + 6].data_ptr();
+    w.post_attn_layernorm_weight = t[base + 7].data_ptr();
+    w.gate_proj_weight = t[base + 8].data_ptr();
+    w.up_proj_weight = t[base + 9].data_ptr();
+    w.down_proj_weight = t[base + 10].data_ptr();
+    return w;
+}
+
+torch::Tensor layer_table(const std::vector<LDGLayerWeights>& host, const torch::Device& dev) {
+    auto cpu = torch::empty({(int64_t)(host.size() * sizeof(LDGLayerWeights))}, torch::kUInt8);
+    std::memcpy(cpu.data_ptr(), host.data(), host.size() * sizeof(LDGLayerWeights));
+    return cpu.to(dev);
+}
+
+[[noreturn]] void raise_engine(int code, uint32_t info, const char* where) {
+    throw std::runtime_error(std::string(where) + ": " + mq_error_string(code) + " (code " + std::to_string(code) +
+                             ", info 0x" + [&] {
+                                 char b[16];
+                                 snprintf(b, sizeof(b), "%x", info);
+                                 return std::string(b);
+                             }() + ")");
+}
+
+// ---------------------------------------------------------------------------
+class MegakernelDecoder {
+public:
+    MegakernelDecoder(torch::Tensor embed_weight, std::vector<torch::Tensor> layer_weights_flat,
+                      torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+                      torch::Tensor sin_table, int num_layers, int max_seq_len)
+        : num_layers_(num_layers), max_seq_len_(max_seq_len) {
+        if (num_layers < 1 || num_layers > MQ_MAX_LAYERS) throw std::runtime_error("num_layers out of range");
+        if (max_seq_len < 1) throw std::runtime_error("max_seq_len must be positive");
+        if ((int)layer_weights_flat.size() != num_layers * 11)
+            throw std::runtime_error("layer_weights_flat must hold num_layers * 11 tensors");
+        check_bf16(embed_weight, "embed_weight", {kVocab, kHidden});
+        check_bf16(final_norm_weight, "final_norm_weight", {kHidden});
+        check_bf16(lm_head_weight, "lm_head_weight", {kVocab, kHidden});
+        if (!cos_table.is_cuda() || cos_table.scalar_type() != torch::kBFloat16 || !cos_table.is_contiguous() ||
+            cos_table.dim() != 2 || cos_table.size(1) != MQ_HEAD_DIM || cos_table.size(0) < max_seq_len)
+            throw std::runtime_error("cos_table must be contiguous bf16 [>=max_seq_len, 128] on the GPU");
+        if (!sin_table.is_cuda() || sin_table.scalar_type() != torch::kBFloat16 || !sin_table.is_contiguous() ||
+            sin_table.sizes() != cos_table.sizes())
+            throw std::runtime_error("sin_table must match cos_table");
+        for (int i = 0; i < num_layers * 11; ++i)
+            check_bf16(layer_weights_flat[i], kLayerNames[i % 11], layer_shape(i % 11));
+        device_ = embed_weight.device();
+        c10::cuda::CUDAGuard guard(device_);
+        embed_ = embed_weight;
+        final_norm_ = final_norm_weight;
+        lm_head_ = lm_head_weight;
+        cos_ = cos_table;
+        sin_ = sin_table;
+        layer_tensors_ = layer_weights_flat;
+        std::vector<LDGLayerWeights> host(num_layers);
+        for (int i = 0; i < num_layers; ++i) host[i] = make_layer(layer_weights_flat, (size_t)i * 11);
+        d_layers_ = layer_table(host, device_);
+        auto bf = torch::dtype(torch::kBFloat16).device(device_);
+        auto f32 = torch::dtype(torch::kFloat32).device(device_);
+        auto i32 = torch::dtype(torch::kInt32).device(device_);
+        k_cache_ = torch::zeros({num_layers, MQ_NUM_KV_HEADS, max_seq_len, MQ_HEAD_DIM}, bf);
+        v_cache_ = torch::zeros({num_layers, MQ_NUM_KV_HEADS, max_seq_len, MQ_HEAD_DIM}, bf);
+        hidden_buffer_ = torch::zeros({kHidden}, bf);
+        g_normalized_ = torch::zeros({kHidden}, f32);
+        output_token_ = torch::zeros({1}, i32);
+        dev_position_ = torch::zeros({1}, i32);
+        workspace_ = torch::zeros({(int64_t)mq_decode_workspace_bytes()}, torch::dtype(torch::kUInt8).device(device_));
+        position_ = 0;
+        attn_scale_ = 1.0f / sqrtf(128.0f);
+    }
+
+    virtual ~MegakernelDecoder() = default;
+
+    int decode_step(int input_token_id) {
+        step(input_token_id, nullptr, nullptr);
+        return last_token_;
+    }
+
+    std::tuple<int, torch::Tensor> decode_step_with_logits(int input_token_id) {
+        auto logits = torch::empty({kVocab}, torch::dtype(torch::kFloat32).device(device_));
+        step(input_token_id, nullptr, logits.data_ptr<float>());
+        return std::make_tuple(last_token_, logits);
+    }
+
+    // Greedy decode of `steps` tokens starting from `first_token` with the token
+    // fed back on the device: no host round trip between steps.  Returns the
+    // generated tokens (device int32 [steps]).
+    torch::Tensor generate_greedy(int first_token, int steps) {
+        if (steps < 0) throw std::runtime_error("steps must be non-negative");
+        if (position_ + steps > max_seq_len_) throw std::runtime_error("generation would exceed max_seq_len");
+        if (first_token < 0 || first_token >= kVocab) throw std::runtime_error("token out of range");
+        c10::cuda::CUDAGuard guard(device_);
+        auto out = torch::empty({steps + 1}, torch::dtype(torch::kInt32).device(device_));
+        out.narrow(0, 0, 1).fill_(first_token);
+        cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
+        for (int i = 0; i < steps; ++i) {
+            mq_decode_params p = params(0, nullptr);
+            p.input_token_ptr = out.data_ptr<int>() + i;
+            p.output_token = out.data_ptr<int>() + i + 1;
+            p.position = position_ + i;
+            int rc = mq_decode(&p, stream);
+            if (rc) raise_engine(rc, 0, "generate_greedy");
+        }
+        check_device("generate_greedy", stream);
+        position_ += steps;
+        return out.narrow(0, 1, steps);
+    }
+
+    void reset() {
+        position_ = 0;
+        k_cache_.zero_();
+        v_cache_.zero_();
+    }
+
+    int position() const { return position_; }
+    void set_position(int p) {
+        if (p < 0 || p > max_seq_len_) throw std::runtime_error("position out of range");
+        position_ = p;
+    }
+    torch::Tensor get_k_cache() const { return k_cache_; }
+    torch::Tensor get_v_cache() const { return v_cache_; }
+    torch::Tensor get_hidden_buffer() const { return hidden_buffer_; }
+    torch::Tensor get_normalized() const { return g_normalized_; }
+    int last_token() const { return last_token_; }
+
+    // Tuning / test hooks
+    void set_num_ctas(int n) { num_ctas_ = n; }
+    void set_attn_chunk(int n) { attn_chunk_ = n; }
+    void set_timeout_ns(long long t) { timeout_ns_ = t; }
+    void set_inject_skip_cta(int c) { inject_skip_cta_ = c; }
+    int num_ctas() const { return num_ctas_ > 0 ? num_ctas_ : mq_decode_default_ctas(); }
+
+    // Raw decode step for benchmarks: token from a device pointer (feedback),
+    // no host synchronisation.  Advances the host position.
+    void decode_step_async(int64_t input_token_ptr, int64_t output_token_ptr) {
+        if (position_ >= max_seq_len_) throw std::runtime_error("position exceeds max_seq_len");
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
+        mq_decode_params p = params(0, nullptr);
+        p.input_token_ptr = reinterpret_cast<const int*>(input_token_ptr);
+        p.output_token = reinterpret_cast<int*>(output_token_ptr);
+        int rc = mq_decode(&p, stream);
+        if (rc) raise_engine(rc, 0, "decode_step_async");
+        position_ += 1;
+    }
+
+    // Reads and clears the device error word; raises if it was set.
+    void check() {
+        c10::cuda::CUDAGuard guard(device_);
+        check_device("check", c10::cuda::getCurrentCUDAStream(device_.index()).stream());
+    }
+
+protected:
+    mq_decode_params params(int token, float* logits) {
+        mq_decode_params p = {};
+        p.input_token = token;
+        p.output_token = output_token_.data_ptr<int>();
+        p.logits = logits;
+        p.embed = embed_.data_ptr();
+        p.layers = reinterpret_cast<const LDGLayerWeights*>(d_layers_.data_ptr());
+        p.final_norm = final_norm_.data_ptr();
+        p.lm_head = lm_head_.data_ptr();
+        p.cos_table = cos_.data_ptr();
+        p.sin_table = sin_.data_ptr();
+        p.k_cache = k_cache_.data_ptr();
+        p.v_cache = v_cache_.data_ptr();
+        p.hidden_out = hidden_buffer_.data_ptr();
+        p.normalized_out = g_normalized_.data_ptr<float>();
+        p.workspace = workspace_.data_ptr();
+        p.workspace_bytes = (size_t)workspace_.numel();
+        p.num_layers = num_layers_;
+        p.position = position_;
+        p.max_seq_len = max_seq_len_;
+        p.attn_scale = attn_scale_;
+        p.num_ctas = num_ctas_;
+        p.attn_chunk = attn_chunk_;
+        p.timeout_ns = timeout_ns_;
+        p.inject_skip_cta = inject_skip_cta_;
+        return p;
+    }
+
+    void check_device(const char* where, cudaStream_t stream) {
+        int tok = 0;
+        uint32_t err = 0, info = 0;
+        int rc = mq_decode_fetch(workspace_.data_ptr(), &tok, &err, &info, stream);
+        if (rc) raise_engine(rc, 0, where);
+        if (err) {
+            mq_decode_workspace_init(workspace_.data_ptr(), (size_t)workspace_.numel(), stream);
+            raise_engine((int)err, info, where);
+        }
+        last_token_ = tok;
+    }
+
+    void step(int input_token_id, const int* token_ptr, float* logits) {
+        if (position_ >= max_seq_len_) throw std::runtime_error("position exceeds max_seq_len");
+        if (!token_ptr && (input_token_id < 0 || input_token_id >= kVocab))
+            throw std::runtime_error("input token out of range");
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
+        mq_decode_params p = params(input_token_id, logits);
+        p.input_token_ptr = token_ptr;
+        int rc = mq_decode(&p, stream);
+        if (rc) raise_engine(rc, 0, "decode_step");
+        check_device("decode_step", stream);
+        position_ += 1;
+    }
+
+    int num_layers_;
+    int max_seq_len_;
+    int position_;
+    float attn_scale_;
+    int last_token_ = -1;
+    int num_ctas_ = 0;
+    int attn_chunk_ = 0;
+    long long timeout_ns_ = 0;
+    int inject_skip_cta_ = 0;
+    torch::Device device_{torch::kCUDA, 0};
+    torch::Tensor embed_, final_norm_, lm_head_, cos_, sin_, d_layers_;
+    std::vector<torch::Tensor> layer_tensors_;
+    torch::Tensor k_cache_, v_cache_, hidden_buffer_, g_normalized_, output_token_, dev_position_, workspace_;
+};
+
+// Prefill + decode.  prefill_step runs the prompt through the decode engine one
+// position at a time with device-side token feed, synchronising once at the
+// end (the reference's cuBLAS prefill, fused_prefill.cu:601-867, computes the
+// same function).
+class MegakernelPrefillDecoder : public MegakernelDecoder {
+public:
+    MegakernelPrefillDecoder(torch::Tensor embed_weight, std::vector<torch::Tensor> layer_weights_flat,
+                             torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+                             torch::Tensor sin_table, int num_layers, int max_seq_len, int max_prefill_len)
+        : MegakernelDecoder(embed_weight, layer_weights_flat, final_norm_weight, lm_head_weight, cos_table,
+                            sin_table, num_layers, max_seq_len),
+          max_prefill_len_(max_prefill_len) {
+        c10::cuda::CUDAGuard guard(device_);
+        input_tokens_ = torch::zeros({std::max(1, max_prefill_len)}, torch::dtype(torch::kInt32).device(device_));
+    }
+
+    int prefill_step(torch::Tensor input_token_ids) {
+        // megakernel_decode.py:496-549: checks, H2D copy, positions 0..S-1.
+        int seq_len = (int)input_token_ids.size(0);
+        if (seq_len > max_prefill_len_) throw std::runtime_error("Prefill sequence length exceeds maximum");
+        if (seq_len == 0) throw std::runtime_error("Empty input sequence");
+        if (seq_len > max_seq_len_) throw std::runtime_error("Prefill sequence length exceeds max_seq_len");
+        c10::cuda::CUDAGuard guard(device_);
+        input_tokens_.narrow(0, 0, seq_len).copy_(input_token_ids.to(torch::kInt32).to(device_));
+        cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
+        auto cpu_ids = input_token_ids.to(torch::kCPU).to(torch::kInt64);
+        auto acc = cpu_ids.accessor<int64_t, 1>();
+        for (int i = 0; i < seq_len; ++i)
+            if (acc[i] < 0 || acc[i] >= kVocab) throw std::runtime_error("input token out of range");
+        for (int i = 0; i < seq_len; ++i) {
+            mq_decode_params p = params(0, nullptr);
+            p.input_token_ptr = input_tokens_.data_ptr<int>() + i;
+            p.position = i;
+            int rc = mq_decode(&p, stream);
+            if (rc) raise_engine(rc, 0, "prefill_step");
+        }
+        check_device("prefill_step", stream);
+        position_ = seq_len;
+        return last_token_;
+    }
+
+    int max_prefill_len() const { return max_prefill_len_; }
+
+protected:
+    int max_prefill_len_;
+    torch::Tensor input_tokens_;
+};
+
+// The reference's GEMV-megakernel prefill class for short prompts
+// (megakernel_decode.py:788-1053): same interface, max_prefill_len 64 by default.
+class MegakernelFusedPrefillDecoder : public MegakernelPrefillDecoder {
+public:
+    using MegakernelPrefillDecoder::MegakernelPrefillDecoder;
+};
+
+// ---------------------------------------------------------------------------
+// chat.py module-function ABI (chat.py:147-323): weights registered in
+// module-level state, caller-owned caches and scratch, reference launchers.
+std::vector<LDGLayerWeights> g_layer_weights;
+torch::Tensor g_d_layer_weights;
+torch::Tensor g_embed_weight;
+std::vector<std::vector<torch::Tensor>> g_keepalive;
+
+void init_ldg_layer_weights(std::vector<torch::Tensor> input_layernorm_weights, std::vector<torch::Tensor> q_proj_weights,
+                            std::vector<torch::Tensor> k_proj_weights, std::vector<torch::Tensor> v_proj_weights,
+                            std::vector<torch::Tensor> q_norm_weights, std::vector<torch::Tensor> k_norm_weights,
+                            std::vector<torch::Tensor> o_proj_weights,
+                            std::vector<torch::Tensor> post_attn_layernorm_weights,
+                            std::vector<torch::Tensor> gate_proj_weights, std::vector<torch::Tensor> up_proj_weights,
+                            std::vector<torch::Tensor> down_proj_weights) {
+    std::vector<std::vector<torch::Tensor>*> lists = {
+        &input_layernorm_weights, &q_proj_weights, &k_proj_weights, &v_proj_weights,
+        &q_norm_weights, &k_norm_weights, &o_proj_weights, &post_attn_layernorm_weights,
+        &gate_proj_weights, &up_proj_weights, &down_proj_weights};
+    size_t L = input_layernorm_weights.size();
+    if (L < 1 || L > MQ_MAX_LAYERS) throw std::runtime_error("number of layers out of range");
+    std::vector<torch::Tensor> flat;
+    for (size_t i = 0; i < L; ++i)
+        for (int k = 0; k < 11; ++k) {
+            if (lists[k]->size() != L) throw std::runtime_error("all eleven weight lists must have the same length");
+            check_bf16((*lists[k])[i], kLayerNames[k], layer_shape(k));
+            flat.push_back((*lists[k])[i]);
+        }
+    g_layer_weights.resize(L);
+    for (size_t i = 0; i < L; ++i) g_layer_weights[i] = make_layer(flat, i * 11);
+    c10::cuda::CUDAGuard guard(flat[0].device());
+    g_d_layer_weights = layer_table(g_layer_weights, flat[0].device());
+    g_keepalive.assign(1, flat);
+}
+
+void init_ldg_embed_weight(torch::Tensor embed_weight) {
+    check_bf16(embed_weight, "embed_weight", {kVocab, kHidden});
+    g_embed_weight = embed_weight;
+}
+
+int decode_ldg_impl(int input_token_id, float* logits, torch::Tensor final_norm_weight, torch::Tensor lm_head_weight,
+                    torch::Tensor cos_table, torch::Tensor sin_table, torch::Tensor k_cache, torch::Tensor v_cache,
+                    torch::Tensor hidden_buffer, torch::Tensor g_activations, torch::Tensor g_residual,
+                    torch::Tensor g_q, torch::Tensor g_k, torch::Tensor g_v, torch::Tensor g_attn_out,
+                    torch::Tensor g_mlp_intermediate, torch::Tensor g_normalized, torch::Tensor block_max_vals,
+                    torch::Tensor block_max_idxs, int num_layers, int position, int cache_len, int max_seq_len) {
+    if (!g_d_layer_weights.defined() || !g_embed_weight.defined())
+        throw std::runtime_error("call init_ldg_layer_weights and init_ldg_embed_weight first");
+    if (num_layers != (int)g_layer_weights.size()) throw std::runtime_error("num_layers does not match the weights");
+    if (position < 0 || position >= max_seq_len) throw std::runtime_error("position exceeds max_seq_len");
+    if (input_token_id < 0 || input_token_id >= kVocab) throw std::runtime_error("input token out of range");
+    check_bf16(k_cache, "k_cache", {num_layers, MQ_NUM_KV_HEADS, max_seq_len, MQ_HEAD_DIM});
+    check_bf16(v_cache, "v_cache", {num_layers, MQ_NUM_KV_HEADS, max_seq_len, MQ_HEAD_DIM});
+    c10::cuda::CUDAGuard guard(k_cache.device());
+    float attn_scale = 1.0f / sqrtf(128.0f);
+    auto output_token = torch::empty({1}, torch::dtype(torch::kInt32).device(k_cache.device()));
+    cudaStream_t stream = c10::cuda::getCurrentCUDAStream(k_cache.device().index()).stream();
+    auto ptr = [](torch::Tensor& t) -> void* { return t.defined() && t.numel() ? t.data_ptr() : nullptr; };
+    if (logits) {
+        launch_ldg_decode_with_logits(input_token_id, output_token.data_ptr<int>(), logits, g_embed_weight.data_ptr(),
+                                      reinterpret_cast<const LDGLayerWeights*>(g_d_layer_weights.data_ptr()),
+                                      final_norm_weight.data_ptr(), lm_head_weight.data_ptr(), cos_table.data_ptr(),
+                                      sin_table.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(),
+                                      ptr(hidden_buffer), ptr(g_activations), ptr(g_residual), ptr(g_q), ptr(g_k),
+                                      ptr(g_v), ptr(g_attn_out), ptr(g_mlp_intermediate), ptr(g_normalized),
+                                      ptr(block_max_vals), ptr(block_max_idxs), num_layers, position, cache_len,
+                                      max_seq_len, attn_scale, stream);
+    } else {
+        launch_ldg_decode(input_token_id, output_token.data_ptr<int>(), g_embed_weight.data_ptr(),
+                          reinterpret_cast<const LDGLayerWeights*>(g_d_layer_weights.data_ptr()),
+                          final_norm_weight.data_ptr(), lm_head_weight.data_ptr(), cos_table.data_ptr(),
+                          sin_table.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), ptr(hidden_buffer),
+                          ptr(g_activations), ptr(g_residual), ptr(g_q), ptr(g_k), ptr(g_v), ptr(g_attn_out),
+                          ptr(g_mlp_intermediate), ptr(g_normalized), ptr(block_max_vals), ptr(block_max_idxs),
+                          num_layers, position, cache_len, max_seq_len, attn_scale, stream);
+    }
+    int rc = mq_get_last_error();
+    if (rc) raise_engine(rc, 0, "decode_ldg");
+    return output_token.item<int>();
+}
+
+int decode_ldg(int input_token_id, torch::Tensor final_norm_weight, torch::Tensor lm_head_weight,
+               torch::Tensor cos_table, torch::Tensor sin_table, torch::Tensor k_cache, torch::Tensor v_cache,
+               torch::Tensor hidden_buffer, torch::Tensor g_activations, torch::Tensor g_residual, torch::Tensor g_q,
+               torch::Tensor g_k, torch::Tensor g_v, torch::Tensor g_attn_out, torch::Tensor g_mlp_intermediate,
+               torch::Tensor g_normalized, torch::Tensor block_max_vals, torch::Tensor block_max_idxs, int num_layers,
+               int position, int cache_len, int max_seq_len) {
+    return decode_ldg_impl(input_token_id, nullptr, final_norm_weight, lm_head_weight, cos_table, sin_table, k_cache,
+                           v_cache, hidden_buffer, g_activations, g_residual, g_q, g_k, g_v, g_attn_out,
+                           g_mlp_intermediate, g_normalized, block_max_vals, block_max_idxs, num_layers, position,
+                           cache_len, max_seq_len);
+}
+
+std::tuple<int, torch::Tensor> decode_ldg_with_logits(
+    int input_token_id, torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+    torch::Tensor sin_table, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor hidden_buffer,
+    torch::Tensor g_activations, torch::Tensor g_residual, torch::Tensor g_q, torch::Tensor g_k, torch::Tensor g_v,
+    torch::Tensor g_attn_out, torch::Tensor g_mlp_intermediate, torch::Tensor g_normalized,
+    torch::Tensor block_max_vals, torch::Tensor block_max_idxs, int num_layers, int position, int cache_len,
+    int max_seq_len) {
+    auto logits = torch::empty({kVocab}, torch::dtype(torch::kFloat32).device(k_cache.device()));
+    int tok = decode_ldg_impl(input_token_id, logits.data_ptr<float>(), final_norm_weight, lm_head_weight, cos_table,
+                              sin_table, k_cache, v_cache, hidden_buffer, g_activations, g_residual, g_q, g_k, g_v,
+                              g_attn_out, g_mlp_intermediate, g_normalized, block_max_vals, block_max_idxs,
+                              num_layers, position, cache_len, max_seq_len);
+    return std::make_tuple(tok, logits);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.doc() = "B200 (sm_100a) Qwen3-0.6B decode engine: reference-compatible torch extension";
+    py::class_<MegakernelDecoder>(m, "MegakernelDecoder")
+        .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
+                      torch::Tensor, int, int>(),
+             py::arg("embed_weight"), py::arg("layer_weights_flat"), py::arg("final_norm_weight"),
+             py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
+             py::arg("max_seq_len"))
+        .def("decode_step", &MegakernelDecoder::decode_step)
+        .def("decode_step_with_logits", &MegakernelDecoder::decode_step_with_logits)
+        .def("generate_greedy", &MegakernelDecoder::generate_greedy)
+        .def("decode_step_async", &MegakernelDecoder::decode_step_async)
+        .def("check", &MegakernelDecoder::check)
+        .def("reset", &MegakernelDecoder::reset)
+        .def("position", &MegakernelDecoder::position)
+        .def("set_position", &MegakernelDecoder::set_position)
+        .def("get_k_cache", &MegakernelDecoder::get_k_cache)
+        .def("get_v_cache", &MegakernelDecoder::get_v_cache)
+        .def("get_hidden_buffer", &MegakernelDecoder::get_hidden_buffer)
+        .def("get_normalized", &MegakernelDecoder::get_normalized)
+        .def("last_token", &MegakernelDecoder::last_token)
+        .def("set_num_ctas", &MegakernelDecoder::set_num_ctas)
+        .def("num_ctas", &MegakernelDecoder::num_ctas)
+        .def("set_attn_chunk", &MegakernelDecoder::set_attn_chunk)
+        .def("set_timeout_ns", &MegakernelDecoder::set_timeout_ns)
+        .def("set_inject_skip_cta", &MegakernelDecoder::set_inject_skip_cta);
+    py::class_<MegakernelPrefillDecoder, MegakernelDecoder>(m, "MegakernelPrefillDecoder")
+        .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
+                      torch::Tensor, int, int, int>(),
+             py::arg("embed_weight"), py::arg("layer_weights_flat"), py::arg("final_norm_weight"),
+             py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
+             py::arg("max_seq_len"), py::arg("max_prefill_len") = 512)
+        .def("prefill_step", &MegakernelPrefillDecoder::prefill_step)
+        .def("max_prefill_len", &MegakernelPrefillDecoder::max_prefill_len);
+    py::class_<MegakernelFusedPrefillDecoder, MegakernelPrefillDecoder>(m, "MegakernelFusedPrefillDecoder")
+        .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
+                      torch::Tensor, int, int, int>(),
+             py::arg("embed_weight"), py::arg("layer_weights_flat"), py::arg("final_norm_weight"),
+             py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
+             py::arg("max_seq_len"), py::arg("max_prefill_len") = 64);
+    m.def("init_ldg_layer_weights", &init_ldg_layer_weights);
+    m.def("init_ldg_embed_weight", &init_ldg_embed_weight);
+    m.def("decode_ldg", &decode_ldg);
+    m.def("decode_ldg_with_logits", &decode_ldg_with_logits);
+    m.def("workspace_bytes", []() { return (int64_t)mq_decode_workspace_bytes(); });
+    m.def("default_ctas", []() { return mq_decode_default_ctas(); });
+    m.def("version", []() { return std::string(mq_version()); });
+}
