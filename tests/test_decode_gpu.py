@@ -64,6 +64,18 @@ def assert_logits_close(got, ref, what=""):
     return err
 
 
+def assert_token_consistent(tok, logits, ref, what=""):
+    """Greedy tokens must agree unless the oracle's top-2 gap is below the
+    logit tolerance actually observed (a genuine near-tie)."""
+    ref_tok = int(torch.argmax(ref).item())
+    if tok == ref_tok:
+        return
+    top2 = torch.topk(ref.float(), 2).values
+    gap = (top2[0] - top2[1]).item()
+    err = (logits.float().cpu() - ref.float()).abs().max().item()
+    assert gap <= 2 * err, f"{what}: token {tok} vs {ref_tok}, top-2 gap {gap}, logits max-abs {err}"
+
+
 def assert_cache_close(dec_cache, ref_cache, upto):
     got = dec_cache[:, :, :upto].cpu()
     ref = ref_cache[:, :, :upto]
@@ -102,15 +114,10 @@ def test_split_k_attention_matches_oracle():
     g = torch.Generator().manual_seed(3)
     toks = torch.randint(0, 151936, (150,), generator=g).tolist()
     for p, t in enumerate(toks):
-        want_logits = p in (0, 7, 8, 9, 63, 64, 65, 100, 149)
-        if want_logits:
-            tok, logits = dec.decode_step_with_logits(t)
-        else:
-            tok = dec.decode_step(t)
+        tok, logits = dec.decode_step_with_logits(t)
         ref = o.decode_step(t, p)
-        if want_logits:
-            assert_logits_close(logits, ref, f"pos={p}")
-        assert tok == int(torch.argmax(ref).item()), f"pos {p}"
+        assert_logits_close(logits, ref, f"pos={p}")
+        assert_token_consistent(tok, logits, ref, f"pos={p}")
     assert_cache_close(dec.get_k_cache(), o.k_cache, len(toks))
 
 
