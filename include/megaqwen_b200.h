@@ -131,6 +131,8 @@ typedef struct mq_decode_params {
     long long timeout_ns;          /* bound on every device wait; 0: default (2 s) */
     int inject_skip_cta;           /* test hook: CTA (value - 1) withholds its layer-0 QKV handoff
                                       stores, so the others' waits run out; 0: off */
+    unsigned long long* trace;     /* optional device buffer [num_ctas * 512] of %globaltimer
+                                      stamps per CTA and phase (profiling); NULL: off */
 } mq_decode_params;
 
 size_t mq_decode_workspace_bytes(void);
@@ -153,6 +155,8 @@ int mq_decode_default_ctas(void);
 /* Last status recorded by the reference-ABI launchers on this host thread. */
 int mq_get_last_error(void);
 const char* mq_error_string(int code);
+/* Text of the last failing CUDA runtime call on this host thread ("" if none). */
+const char* mq_last_error_detail(void);
 /* Library version string. */
 const char* mq_version(void);
 

@@ -15,7 +15,7 @@ try:
     from . import _C  # type: ignore[attr-defined]
 except ImportError as exc:  # pragma: no cover - exercised only on broken installs
     raise ImportError(
-        "megaqwen_b200 native extension is not built; run `python -m megaqwen_b200.build`"
+        "megaqwen_b200 native extension is not built; run `python megaqwen_b200/build.py`"
     ) from exc
 
 MegakernelDecoder = _C.MegakernelDecoder

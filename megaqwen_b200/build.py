@@ -9,7 +9,7 @@ Outputs
 ``megaqwen_b200/_C<ext-suffix>``           the torch extension exposing the
     reference's classes, linked against the library above.
 
-Run ``python -m megaqwen_b200.build`` (or ``__graft_entry__.build()``).  Each
+Run ``python megaqwen_b200/build.py`` (or ``__graft_entry__.build()``).  Each
 output is rebuilt only when a source it depends on is newer.
 """
 from __future__ import annotations

@@ -37,6 +37,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 #include <vector>
 
@@ -57,7 +58,7 @@ constexpr int KVS = NKV * D;               // 1024
 constexpr int QKV = QS + 2 * KVS;          // 4096
 constexpr int V = MQ_VOCAB_SIZE;           // 151936
 
-constexpr int NCW = 16;                    // consumer warps
+constexpr int NCW = 15;                    // consumer warps (16 warps in all: 128 registers per thread)
 constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + one producer warp
 constexpr int STAGE_BYTES = 32768;
@@ -66,16 +67,19 @@ constexpr int MAX_CTAS = 256;
 constexpr int CMAX = MAX_CTAS / NKV;       // max position chunks per kv head
 constexpr int PART_STRIDE = 132;           // floats per (unit, head): m, l, pad, pad, acc[128]
 
-constexpr int QKV_TILE = STAGE_BYTES / (H * 2);      // 16 rows
-constexpr int O_TILE = STAGE_BYTES / (QS * 2);       // 8 rows
-constexpr int GU_TILE = STAGE_BYTES / (2 * H * 2);   // 8 gate+up row pairs
-constexpr int DOWN_TILE = STAGE_BYTES / (I * 2);     // 5 rows
-constexpr int LM_TILE = STAGE_BYTES / (H * 2);       // 16 rows
+constexpr int cmin(int a, int b) { return a < b ? a : b; }
+constexpr int QKV_TILE = cmin(NCW, STAGE_BYTES / (H * 2));      // 15 rows
+constexpr int O_TILE = cmin(NCW, STAGE_BYTES / (QS * 2));       // 8 rows
+constexpr int GU_TILE = cmin(NCW, STAGE_BYTES / (2 * H * 2));   // 8 gate+up row pairs
+constexpr int DOWN_TILE = cmin(NCW, STAGE_BYTES / (I * 2));     // 5 rows
+constexpr int LM_TILE = cmin(NCW, STAGE_BYTES / (H * 2));       // 15 rows
+constexpr int HPT = (H + NCT - 1) / NCT;             // hidden elements per consumer thread (3)
 constexpr int KV_TILE = STAGE_BYTES / (2 * D * 2);   // 64 positions (K and V)
 static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <= NCW && LM_TILE <= NCW,
               "one consumer warp per row of a tile");
 
-constexpr int BAR_CONSUMERS = 1;           // named barrier id for the consumer warps
+constexpr int BAR_CONSUMERS = 1;
+constexpr int TRACE_STRIDE = 2048;        // trace slots per CTA: phases [0,512), tiles [512, 2012)           // named barrier id for the consumer warps
 
 // ---- workspace layout (bytes) ------------------------------------------------
 struct Control {
@@ -115,7 +119,9 @@ constexpr int SM_RED = SM_ML + NCW * 4 * 4;               // fp32 [2][16]
 constexpr int SM_BEST = SM_RED + 2 * NCW * 4;             // fp32 [16] + int [16]
 constexpr int SM_FLAGS = SM_BEST + 2 * NCW * 4;           // int [4]
 constexpr int SM_BARS = SM_FLAGS + 16;                    // uint64 full[NSTAGES], empty[NSTAGES]
-constexpr int SMEM_BYTES = SM_BARS + 2 * NSTAGES * 8;
+constexpr int SM_LAYERS = SM_BARS + 2 * NSTAGES * 8;      // LDGLayerWeights [num_layers] copy
+constexpr int SM_SCHED = SM_LAYERS + MQ_MAX_LAYERS * (int)sizeof(LDGLayerWeights);  // Sched
+constexpr int SMEM_BYTES = SM_SCHED + 128;
 static_assert(SM_ACC + NCW * 2 * D * 4 <= SM_H, "attention combine scratch fits in X+H2");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(SM_BARS % 8 == 0, "mbarrier alignment");
@@ -146,6 +152,12 @@ struct KParams {
     int attn_chunk;
     long long timeout_ns;
     int inject_skip_cta;
+    unsigned long long* trace;
+    int poll_mode;
+    int poll_warps;
+    int poll_sleep_ns;
+    int arrive_relaxed;
+    int store_mode;
 };
 
 // Per-CTA slice of every phase (identical on the producer and consumer side).
@@ -156,6 +168,15 @@ struct Sched {
     int qkv_a, qkv_b, o_a, o_b, gu_a, gu_b, dn_a, dn_b, lm_a, lm_b;
     int has_unit, ug, uj, C, kv_s, kv_e, last;
 };
+
+static_assert(sizeof(Sched) <= 128, "Sched fits its shared-memory slot");
+
+// Dynamic shared memory of the decode kernel.  Everything a CTA keeps on chip
+// is addressed from this base with the SM_* offsets above, so no pointer to it
+// occupies a register.
+extern __shared__ __align__(1024) uint8_t g_smem[];
+template <typename T>
+__device__ __forceinline__ T* sm(int off) { return reinterpret_cast<T*>(g_smem + off); }
 
 __device__ __forceinline__ int split_at(int n, int G, int c) { return (int)(((long long)c * n) / G); }
 
@@ -209,66 +230,70 @@ __device__ __forceinline__ float dot8(uint4 w, float4 lo, float4 hi) {
     return s;
 }
 
-// ---- the per-CTA tile walk, shared by producer and consumers --------------------
-template <class Vis>
-__device__ __forceinline__ void walk(const KParams& P, const Sched& S, Vis& v) {
-    for (int l = 0; l < P.num_layers; ++l) {
-        const LDGLayerWeights* W = P.layers + l;
-        const char* wq = (const char*)W->q_proj_weight;
-        const char* wk = (const char*)W->k_proj_weight;
-        const char* wv = (const char*)W->v_proj_weight;
-        const char* wo = (const char*)W->o_proj_weight;
-        const char* wg = (const char*)W->gate_proj_weight;
-        const char* wu = (const char*)W->up_proj_weight;
-        const char* wd = (const char*)W->down_proj_weight;
-
-        if (!v.begin(PH_QKV, l)) return;
+// ---- the per-CTA tile lists, shared by producer and consumers ------------------
+// for_tiles calls f(first_row, rows, src1, bytes1, src2, bytes2) for every
+// stage-sized tile this CTA owns in one phase of one layer, in ring order.
+template <class F>
+__device__ __forceinline__ void for_tiles(const KParams& P, const Sched& S, int phase, int l, F&& f) {
+    if (phase == PH_LM) {
+        for (int r = S.lm_a; r < S.lm_b;) {
+            int n = min(S.lm_b - r, LM_TILE);
+            f(r, n, (const char*)P.lm_head + (size_t)r * H * 2, n * H * 2, (const char*)nullptr, 0);
+            r += n;
+        }
+        return;
+    }
+    const LDGLayerWeights& W = sm<LDGLayerWeights>(SM_LAYERS)[l];
+    if (phase == PH_QKV) {
         for (int r = S.qkv_a; r < S.qkv_b;) {
             const char* base;
             int r0, lim;
-            if (r < QS) { base = wq; r0 = r; lim = QS; }
-            else if (r < QS + KVS) { base = wk; r0 = r - QS; lim = QS + KVS; }
-            else { base = wv; r0 = r - QS - KVS; lim = QKV; }
+            if (r < QS) { base = (const char*)W.q_proj_weight; r0 = r; lim = QS; }
+            else if (r < QS + KVS) { base = (const char*)W.k_proj_weight; r0 = r - QS; lim = QS + KVS; }
+            else { base = (const char*)W.v_proj_weight; r0 = r - QS - KVS; lim = QKV; }
             int n = min(min(S.qkv_b, lim) - r, QKV_TILE);
-            v.tile(PH_QKV, l, r, n, base + (size_t)r0 * H * 2, n * H * 2, nullptr, 0);
+            f(r, n, base + (size_t)r0 * H * 2, n * H * 2, (const char*)nullptr, 0);
             r += n;
         }
-        if (S.has_unit) {
-            if (!v.begin(PH_ATTN, l)) return;
-            for (int t = S.kv_s; t < S.kv_e; t += KV_TILE) {
-                int n = min(S.kv_e - t, KV_TILE);
-                size_t off = (((size_t)l * NKV + S.ug) * P.max_seq_len + t) * D * 2;
-                v.tile(PH_ATTN, l, t, n, (const char*)P.k_cache + off, n * D * 2, (const char*)P.v_cache + off,
-                       n * D * 2);
-            }
-            v.end_attn(l);
+    } else if (phase == PH_ATTN) {
+        for (int t = S.kv_s; t < S.kv_e; t += KV_TILE) {
+            int n = min(S.kv_e - t, KV_TILE);
+            size_t off = (((size_t)l * NKV + S.ug) * P.max_seq_len + t) * D * 2;
+            f(t, n, (const char*)P.k_cache + off, n * D * 2, (const char*)P.v_cache + off, n * D * 2);
         }
-        if (!v.begin(PH_O, l)) return;
+    } else if (phase == PH_O) {
         for (int r = S.o_a; r < S.o_b;) {
             int n = min(S.o_b - r, O_TILE);
-            v.tile(PH_O, l, r, n, wo + (size_t)r * QS * 2, n * QS * 2, nullptr, 0);
+            f(r, n, (const char*)W.o_proj_weight + (size_t)r * QS * 2, n * QS * 2, (const char*)nullptr, 0);
             r += n;
         }
-        if (!v.begin(PH_GU, l)) return;
+    } else if (phase == PH_GU) {
         for (int r = S.gu_a; r < S.gu_b;) {
             int n = min(S.gu_b - r, GU_TILE);
-            v.tile(PH_GU, l, r, n, wg + (size_t)r * H * 2, n * H * 2, wu + (size_t)r * H * 2, n * H * 2);
+            f(r, n, (const char*)W.gate_proj_weight + (size_t)r * H * 2, n * H * 2,
+              (const char*)W.up_proj_weight + (size_t)r * H * 2, n * H * 2);
             r += n;
         }
-        if (!v.begin(PH_DOWN, l)) return;
+    } else {
         for (int r = S.dn_a; r < S.dn_b;) {
             int n = min(S.dn_b - r, DOWN_TILE);
-            v.tile(PH_DOWN, l, r, n, wd + (size_t)r * I * 2, n * I * 2, nullptr, 0);
+            f(r, n, (const char*)W.down_proj_weight + (size_t)r * I * 2, n * I * 2, (const char*)nullptr, 0);
             r += n;
         }
     }
-    if (!v.begin(PH_LM, P.num_layers)) return;
-    for (int r = S.lm_a; r < S.lm_b;) {
-        int n = min(S.lm_b - r, LM_TILE);
-        v.tile(PH_LM, P.num_layers, r, n, (const char*)P.lm_head + (size_t)r * H * 2, n * H * 2, nullptr, 0);
-        r += n;
+}
+
+// The per-token phase sequence of one CTA.
+template <class Vis>
+__device__ __forceinline__ void walk(const KParams& P, const Sched& S, Vis& v) {
+    for (int l = 0; l < P.num_layers; ++l) {
+        if (!v.run(PH_QKV, l)) return;
+        if (S.has_unit && !v.run(PH_ATTN, l)) return;
+        if (!v.run(PH_O, l)) return;
+        if (!v.run(PH_GU, l)) return;
+        if (!v.run(PH_DOWN, l)) return;
     }
-    v.end_lm();
+    v.run(PH_LM, P.num_layers);
 }
 
 // ---- producer: one thread issuing bulk copies into the stage ring ---------------
@@ -288,11 +313,13 @@ struct Producer {
         flags = reinterpret_cast<volatile int*>(s + SM_FLAGS);
         policy = policy_evict_first();
     }
-    __device__ bool begin(int, int) { return ok; }
-    __device__ void end_attn(int) {}
-    __device__ void end_lm() {}
+    __device__ __forceinline__ bool run(int phase, int l) {
+        for_tiles(P, *sm<Sched>(SM_SCHED), phase, l,
+                  [&](int, int, const char* s1, int b1, const char* s2, int b2) { tile(phase, l, s1, b1, s2, b2); });
+        return ok;
+    }
 
-    __device__ void tile(int phase, int layer, int, int, const char* src1, int b1, const char* src2, int b2) {
+    __device__ __forceinline__ void tile(int phase, int layer, const char* src1, int b1, const char* src2, int b2) {
         if (!ok) return;
         const uint32_t s = n % NSTAGES;
         if (n >= (uint32_t)NSTAGES) {
@@ -313,6 +340,7 @@ struct Producer {
             }
         }
         uint8_t* dst = smem + SM_STAGES + s * STAGE_BYTES;
+        if (P.trace && n < 320) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 512 + 4 * n] = globaltimer_ns();
         mbar_arrive_expect_tx(&full[s], (uint32_t)(b1 + b2));
         bulk_g2s(dst, src1, (uint32_t)b1, &full[s], policy);
         if (b2) bulk_g2s(dst + b1, src2, (uint32_t)b2, &full[s], policy);
@@ -320,7 +348,7 @@ struct Producer {
     }
 
     // Wait (bounded) for every issued copy to land before the CTA may exit.
-    __device__ void drain() {
+    __device__ __forceinline__ void drain() {
         uint32_t first = n > (uint32_t)NSTAGES ? n - NSTAGES : 0;
         for (uint32_t k = first; k < n; ++k) {
             const uint32_t s = k % NSTAGES, par = (k / NSTAGES) & 1u;
@@ -332,60 +360,58 @@ struct Producer {
     }
 };
 
+// Online-softmax state of one attention work unit (two q heads of one kv
+// head); each lane owns head dims 4*lane .. 4*lane+3.
+struct AttnState {
+    float q0[4], q1[4], a0[4], a1[4];
+    float m0, l0, m1, l1;
+};
+
+// Running LM-head argmax of one warp (value, then lowest index on ties).
+struct LmBest {
+    float v;
+    int i;
+};
+
 // ---- consumers: 16 warps computing on staged tiles -------------------------------
 struct Consumer {
     const KParams& P;
     const Sched& S;
-    uint8_t* smem;
-    uint64_t* full;
-    uint64_t* empty;
-    volatile int* flags;
-    float* sx;
-    float* sh;
-    float* sh2;
-    float* sred;
     int ct, warp, lane;
     uint32_t n = 0;          // tiles consumed
     bool ok = true;          // this thread's view; made collective at begin()
     int red_par = 0;
-    float xr[32];            // this lane's slice of a K=1024 input vector
-    // attention state: two q heads of one kv head; lane owns dims 4*lane..4*lane+3
-    float q0[4], q1[4], a0[4], a1[4];
-    float m0, l0, m1, l1;
-    // LM-head running best (lane 0 of each warp)
-    float best_v;
-    int best_i;
 
-    __device__ Consumer(const KParams& p, const Sched& s, uint8_t* sm) : P(p), S(s), smem(sm) {
-        full = reinterpret_cast<uint64_t*>(sm + SM_BARS);
-        empty = full + NSTAGES;
-        flags = reinterpret_cast<volatile int*>(sm + SM_FLAGS);
-        sx = reinterpret_cast<float*>(sm + SM_X);
-        sh = reinterpret_cast<float*>(sm + SM_H);
-        sh2 = reinterpret_cast<float*>(sm + SM_H2);
-        sred = reinterpret_cast<float*>(sm + SM_RED);
+    __device__ static float* sx() { return sm<float>(SM_X); }
+    __device__ static float* sh() { return sm<float>(SM_H); }
+    __device__ static float* sh2() { return sm<float>(SM_H2); }
+    __device__ static float* sred() { return sm<float>(SM_RED); }
+    __device__ static uint64_t* full() { return sm<uint64_t>(SM_BARS); }
+    __device__ static uint64_t* empty() { return sm<uint64_t>(SM_BARS) + NSTAGES; }
+    __device__ static volatile int* flags() { return sm<volatile int>(SM_FLAGS); }
+
+    __device__ Consumer(const KParams& p, const Sched& s) : P(p), S(s) {
         ct = threadIdx.x - 32;
         warp = ct >> 5;
         lane = ct & 31;
-        best_v = -INFINITY;
-        best_i = 0x7fffffff;
     }
 
-    __device__ void fail(uint32_t code, uint32_t info) {
+    __device__ __forceinline__ void fail(uint32_t code, uint32_t info) {
         if (ok) {
             if (!global_error(P)) record_error(P, code, info);
-            flags[0] = 1;
+            flags()[0] = 1;
         }
         ok = false;
     }
 
     // Poll n tagged words src[idx] (idx = ct + k*NCT, k < 8) into vals; bounded.
-    __device__ int poll(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info) {
+    __device__ __forceinline__ int poll(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info) {
         int cnt = 0;
         uint32_t pending = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
             if (ct + k * NCT < count) { pending |= 1u << k; cnt = k + 1; }
+        if (P.poll_mode == 2) return poll_few(src, count, tag, vals, info, cnt);
         if (!ok) return cnt;
         uint64_t t0 = 0;
         uint32_t spins = 0;
@@ -400,110 +426,174 @@ struct Consumer {
                     vals[k] = __uint_as_float((uint32_t)w[k]);
                     pending &= ~(1u << k);
                 }
+            if (pending && P.poll_mode == 1) __nanosleep(P.poll_sleep_ns);
             if (pending && ((++spins & 31u) == 0)) {
                 uint64_t now = globaltimer_ns();
                 if (t0 == 0) t0 = now;
-                if (flags[0] != 0 || global_error(P)) { ok = false; break; }
+                if (flags()[0] != 0 || global_error(P)) { ok = false; break; }
                 if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, info); break; }
             }
         }
         return cnt;
     }
 
+    // Poll with only the first P.poll_warps warps, staging values through X.
+    __device__ __forceinline__ int poll_few(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info, int cnt) {
+        named_bar_sync(BAR_CONSUMERS, NCT);  // previous phase is done with X
+        const int pw = P.poll_warps;
+        if (warp < pw && ok) {
+            const int stride = pw * 32;
+            const int me = warp * 32 + lane;
+            uint64_t t0 = 0;
+            uint32_t spins = 0;
+            for (int base = 0; base < count && ok; base += 8 * stride) {
+                uint32_t pending = 0;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+                    if (base + me + k * stride < count) pending |= 1u << k;
+                while (pending) {
+                    uint64_t w[8];
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if (pending & (1u << k)) w[k] = ld_relaxed_u64(src + base + me + k * stride);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k)
+                        if ((pending & (1u << k)) && (uint32_t)(w[k] >> 32) == tag) {
+                            sx()[base + me + k * stride] = __uint_as_float((uint32_t)w[k]);
+                            pending &= ~(1u << k);
+                        }
+                    if (pending && P.poll_sleep_ns) __nanosleep(P.poll_sleep_ns);
+                    if (pending && ((++spins & 31u) == 0)) {
+                        uint64_t now = globaltimer_ns();
+                        if (t0 == 0) t0 = now;
+                        if (flags()[0] != 0 || global_error(P)) { ok = false; break; }
+                        if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, info); break; }
+                    }
+                }
+            }
+        }
+        named_bar_sync(BAR_CONSUMERS, NCT);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (k < cnt) vals[k] = sx()[ct + k * NCT];
+        return cnt;
+    }
+
+    __device__ __forceinline__ void ll_store(uint64_t* p, uint64_t w) {
+        if (P.store_mode == 1) asm volatile("st.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+        else if (P.store_mode == 2) asm volatile("st.global.cg.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+        else if (P.store_mode == 3) asm volatile("st.volatile.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+        else st_relaxed_u64(p, w);
+    }
+
     // Collective: all consumer threads agree on failure.
-    __device__ bool agree() {
+    __device__ __forceinline__ bool agree() {
         bool bad = named_bar_or(BAR_CONSUMERS, NCT, !ok);
         if (bad) ok = false;
         return !bad;
     }
 
-    __device__ float block_sum(float v) {
+    __device__ __forceinline__ float block_sum(float v) {
         // caller guarantees a barrier separates consecutive uses of one parity
-        float* r = sred + red_par * NCW;
+        float* r = sred() + red_par * NCW;
         red_par ^= 1;
         v = warp_sum(v);
         if (lane == 0) r[warp] = v;
         return 0.f;  // the total is read after the next barrier via read_sum()
     }
-    __device__ float read_sum() {
-        const float* r = sred + (red_par ^ 1) * NCW;
+    __device__ __forceinline__ float read_sum() {
+        const float* r = sred() + (red_par ^ 1) * NCW;
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < NCW; ++i) s += r[i];
         return s;
     }
 
-    // Store this thread's normalized K=1024 vector elements into X (planar) and
-    // then load the lane's register slice.  v[k] holds element ct + k*NCT.
-    __device__ void publish_norm_1024(const float* v, float rstd, const bf16* w) {
+    // Store this thread's normalized K=1024 vector elements into X (planar).
+    // v[k] holds element ct + k*NCT.
+    __device__ __forceinline__ void publish_norm_1024(const float* v, float rstd, const float* wv) {
 #pragma unroll
-        for (int k = 0; k < 2; ++k) {
+        for (int k = 0; k < HPT; ++k) {
             int i = ct + k * NCT;
-            sx[planar_index(i, H)] = v[k] * rstd * __bfloat162float(w[i]);
+            if (i < H) sx()[planar_index(i, H)] = v[k] * rstd * wv[k];
         }
         named_bar_sync(BAR_CONSUMERS, NCT);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            int c = lane + 32 * u;
-            float4 lo = *reinterpret_cast<const float4*>(sx + c * 4);
-            float4 hi = *reinterpret_cast<const float4*>(sx + H / 2 + c * 4);
-            xr[u * 8 + 0] = lo.x; xr[u * 8 + 1] = lo.y; xr[u * 8 + 2] = lo.z; xr[u * 8 + 3] = lo.w;
-            xr[u * 8 + 4] = hi.x; xr[u * 8 + 5] = hi.y; xr[u * 8 + 6] = hi.z; xr[u * 8 + 7] = hi.w;
-        }
     }
 
-    __device__ bool begin(int phase, int l) {
+    // Optional per-phase timestamps (profiling): slot (l*6+phase)*2 on entry,
+    // +1 once the phase's input vector has arrived.
+    template <int KIND>
+    __device__ __forceinline__ bool begin(int phase, int l) {
+        const bool tr = P.trace != nullptr && ct == 0;
+        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + (l * 6 + phase) * 2] = globaltimer_ns();
+        bool r = begin_impl<KIND>(phase, l);
+        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + (l * 6 + phase) * 2 + 1] = globaltimer_ns();
+        return r;
+    }
+
+    __device__ __forceinline__ const LDGLayerWeights& layer(int l) const {
+        return reinterpret_cast<const LDGLayerWeights*>(g_smem + SM_LAYERS)[l];
+    }
+
+    // Every load that does not depend on the polled vector (norm weights, RoPE
+    // rows) is issued before the poll so its latency overlaps the wait.
+    template <int KIND>
+    __device__ __forceinline__ bool begin_impl(int phase, int l) {
         float v[8];
-        if (phase == PH_QKV || phase == PH_LM) {
-            // Layer input h: the embedding row (layer 0) or the previous layer's output.
-            if (l == 0) {
-                const bf16* row = P.embed + (size_t)flags[1] * H;
-                v[0] = __bfloat162float(row[ct]);
-                v[1] = __bfloat162float(row[ct + NCT]);
+        if (KIND == 0 || KIND == 2) {
+            const bf16* w = (phase == PH_LM)  ? P.final_norm
+                            : (phase == PH_GU) ? (const bf16*)layer(l).post_attn_layernorm_weight
+                                               : (const bf16*)layer(l).input_layernorm_weight;
+            float wv[HPT];
+#pragma unroll
+            for (int k = 0; k < HPT; ++k) {
+                v[k] = 0.f;
+                wv[k] = (ct + k * NCT < H) ? __bfloat162float(w[ct + k * NCT]) : 0.f;
+            }
+            // QKV/LM: layer input h (embedding row at layer 0, else the previous
+            // layer's output); GU: the post-attention residual.
+            if (phase == PH_GU) {
+                poll(ll_hmid(P, l), H, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
+            } else if (l == 0) {
+                const bf16* row = P.embed + (size_t)flags()[1] * H;
+#pragma unroll
+                for (int k = 0; k < HPT; ++k)
+                    if (ct + k * NCT < H) v[k] = __bfloat162float(row[ct + k * NCT]);
             } else {
                 poll(ll_hout(P, l - 1), H, tag_of(S, l - 1), v, ((uint32_t)phase << 8) | l);
             }
-            if (ok) {
-                sh[ct] = v[0];
-                sh[ct + NCT] = v[1];
-            }
-            block_sum(v[0] * v[0] + v[1] * v[1]);
+            float* res = (phase == PH_GU) ? sh2() : sh();
+            float ss = 0.f;
+#pragma unroll
+            for (int k = 0; k < HPT; ++k)
+                if (ct + k * NCT < H) {
+                    if (ok) res[ct + k * NCT] = v[k];
+                    ss += v[k] * v[k];
+                }
+            block_sum(ss);
             if (!agree()) return false;
             float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
-            const bf16* w = (phase == PH_LM) ? P.final_norm : (const bf16*)P.layers[l].input_layernorm_weight;
             if (phase == PH_LM && S.c == 0) {
-                if (P.hidden_out) {
-                    P.hidden_out[ct] = __float2bfloat16(v[0]);
-                    P.hidden_out[ct + NCT] = __float2bfloat16(v[1]);
-                }
-                if (P.norm_out) {
-                    P.norm_out[ct] = v[0] * rstd * __bfloat162float(w[ct]);
-                    P.norm_out[ct + NCT] = v[1] * rstd * __bfloat162float(w[ct + NCT]);
+#pragma unroll
+                for (int k = 0; k < HPT; ++k) {
+                    const int i = ct + k * NCT;
+                    if (i >= H) continue;
+                    if (P.hidden_out) P.hidden_out[i] = __float2bfloat16(v[k]);
+                    if (P.norm_out) P.norm_out[i] = v[k] * rstd * wv[k];
                 }
             }
-            publish_norm_1024(v, rstd, w);
+            publish_norm_1024(v, rstd, wv);
             return true;
         }
-        if (phase == PH_GU) {
-            poll(ll_hmid(P, l), H, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
-            if (ok) {
-                sh2[ct] = v[0];
-                sh2[ct + NCT] = v[1];
-            }
-            block_sum(v[0] * v[0] + v[1] * v[1]);
-            if (!agree()) return false;
-            float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
-            publish_norm_1024(v, rstd, (const bf16*)P.layers[l].post_attn_layernorm_weight);
-            return true;
-        }
-        if (phase == PH_O || phase == PH_DOWN) {
+        if (KIND == 3) {
             const int K = (phase == PH_O) ? QS : I;
             const uint64_t* src = (phase == PH_O) ? ll_attn(P, l) : ll_act(P, l);
             int cnt = poll(src, K, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
             if (!agree()) return false;
-            for (int k = 0; k < cnt; ++k) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
                 int i = ct + k * NCT;
-                if (i < K) sx[planar_index(i, K)] = v[k];
+                if (k < cnt && i < K) sx()[planar_index(i, K)] = v[k];
             }
             named_bar_sync(BAR_CONSUMERS, NCT);
             return true;
@@ -512,37 +602,64 @@ struct Consumer {
         {
             const int g = S.ug;
             const uint64_t* src = ll_qkv(P, l);
-            float* raw = reinterpret_cast<float*>(smem + SM_QKVRAW);
-            // 512 words: q rows [256g, 256g+256), k rows [2048+128g, +128), v rows [3072+128g, +128)
-            int idx = ct < 256 ? 256 * g + ct : (ct < 384 ? QS + 128 * g + (ct - 256) : QS + KVS + 128 * g + (ct - 384));
-            float val = 0.f;
+            float* raw = reinterpret_cast<float*>(g_smem + SM_QKVRAW);
+            const LDGLayerWeights& W = layer(l);
+            // warps 0,1: q heads 2g, 2g+1; warp 2: k head g.  Lane owns elements
+            // lane + 32m (m = 0..3); rotate-half pairs (m, m+2) stay in the lane.
+            float nwv[4], csv[4], snv[4];
+            if (warp < 3) {
+                const bf16* nw = (const bf16*)(warp < 2 ? W.q_norm_weight : W.k_norm_weight);
+                const bf16* cs = P.cos_table + (size_t)S.pos * D;
+                const bf16* sn = P.sin_table + (size_t)S.pos * D;
+#pragma unroll
+                for (int m = 0; m < 4; ++m) {
+                    nwv[m] = __bfloat162float(nw[lane + 32 * m]);
+                    csv[m] = __bfloat162float(cs[lane + 32 * m]);
+                    snv[m] = __bfloat162float(sn[lane + 32 * m]);
+                }
+            }
+            // 512 words: q rows [256g, 256g+256), k rows [2048+128g, +128), v rows [3072+128g, +128);
+            // thread ct polls words j = ct and j = ct + NCT (j < 512).
+            float val[2] = {0.f, 0.f};
             if (ok) {
                 uint64_t t0 = 0;
                 uint32_t spins = 0;
                 const uint32_t tag = tag_of(S, l);
-                while (true) {
-                    uint64_t w = ld_relaxed_u64(src + idx);
-                    if ((uint32_t)(w >> 32) == tag) { val = __uint_as_float((uint32_t)w); break; }
-                    if ((++spins & 31u) == 0) {
+                uint32_t pending = 1u | ((ct + NCT < 512) ? 2u : 0u);
+                int idx[2];
+#pragma unroll
+                for (int k = 0; k < 2; ++k) {
+                    const int j = ct + k * NCT;
+                    idx[k] = j < 256 ? 256 * g + j : (j < 384 ? QS + 128 * g + (j - 256) : QS + KVS + 128 * g + (j - 384));
+                }
+                while (pending) {
+                    uint64_t w[2];
+#pragma unroll
+                    for (int k = 0; k < 2; ++k)
+                        if (pending & (1u << k)) w[k] = ld_relaxed_u64(src + idx[k]);
+#pragma unroll
+                    for (int k = 0; k < 2; ++k)
+                        if ((pending & (1u << k)) && (uint32_t)(w[k] >> 32) == tag) {
+                            val[k] = __uint_as_float((uint32_t)w[k]);
+                            pending &= ~(1u << k);
+                        }
+                    if (pending && (++spins & 31u) == 0) {
                         uint64_t now = globaltimer_ns();
                         if (t0 == 0) t0 = now;
-                        if (flags[0] != 0 || global_error(P)) { ok = false; break; }
+                        if (flags()[0] != 0 || global_error(P)) { ok = false; break; }
                         if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, (1u << 8) | l); break; }
                     }
                 }
             }
             if (!agree()) return false;
-            raw[ct] = val;
+            raw[ct] = val[0];
+            if (ct + NCT < 512) raw[ct + NCT] = val[1];
             named_bar_sync(BAR_CONSUMERS, NCT);
-            float* qn = reinterpret_cast<float*>(smem + SM_QN);
-            float* kp = reinterpret_cast<float*>(smem + SM_KP);
-            float* vp = reinterpret_cast<float*>(smem + SM_VP);
-            const LDGLayerWeights* W = P.layers + l;
+            float* qn = reinterpret_cast<float*>(g_smem + SM_QN);
+            float* kp = reinterpret_cast<float*>(g_smem + SM_KP);
+            float* vp = reinterpret_cast<float*>(g_smem + SM_VP);
             if (warp < 3) {
-                // warps 0,1: q heads 2g, 2g+1; warp 2: k head g.  Lane owns elements
-                // lane + 32m (m = 0..3); rotate-half pairs (m, m+2) stay in the lane.
                 const float* x = raw + (warp < 2 ? warp * D : 256);
-                const bf16* nw = (const bf16*)(warp < 2 ? W->q_norm_weight : W->k_norm_weight);
                 float e[4];
                 float ss = 0.f;
 #pragma unroll
@@ -550,14 +667,11 @@ struct Consumer {
                 ss = warp_sum(ss);
                 float r = rsqrtf(ss / (float)D + 1e-6f);
 #pragma unroll
-                for (int m = 0; m < 4; ++m) e[m] = e[m] * r * __bfloat162float(nw[lane + 32 * m]);
-                const bf16* cs = P.cos_table + (size_t)S.pos * D;
-                const bf16* sn = P.sin_table + (size_t)S.pos * D;
+                for (int m = 0; m < 4; ++m) e[m] = e[m] * r * nwv[m];
                 float o[4];
 #pragma unroll
                 for (int m = 0; m < 4; ++m) {
-                    int i = lane + 32 * m;
-                    float c = __bfloat162float(cs[i]), s = __bfloat162float(sn[i]);
+                    float c = csv[m], s = snv[m];
                     o[m] = (m < 2) ? (e[m] * c - e[m + 2] * s) : (e[m] * c + e[m - 2] * s);
                 }
                 if (warp < 2) {
@@ -583,31 +697,22 @@ struct Consumer {
                 }
             }
             named_bar_sync(BAR_CONSUMERS, NCT);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                q0[i] = qn[4 * lane + i] * P.attn_scale;
-                q1[i] = qn[D + 4 * lane + i] * P.attn_scale;
-                a0[i] = 0.f;
-                a1[i] = 0.f;
-            }
-            m0 = m1 = -INFINITY;
-            l0 = l1 = 0.f;
             return true;
         }
     }
 
     // Warp-uniform bounded wait for stage s to fill (all lanes iterate together).
-    __device__ bool wait_full(uint32_t s, uint32_t par, int phase, int l) {
+    __device__ __forceinline__ bool wait_full(uint32_t s, uint32_t par, int phase, int l) {
         if (!ok) return false;
         uint64_t t0 = 0;
         uint32_t spins = 0;
-        while (!__all_sync(0xffffffffu, mbar_try_wait(&full[s], par))) {
+        while (!__all_sync(0xffffffffu, mbar_try_wait(&full()[s], par))) {
             if ((++spins & 63u) == 0) {
                 int verdict = 0;
                 if (lane == 0) {
                     uint64_t now = globaltimer_ns();
                     if (t0 == 0) t0 = now;
-                    if (flags[0] != 0 || global_error(P)) verdict = 1;
+                    if (flags()[0] != 0 || global_error(P)) verdict = 1;
                     else if ((long long)(now - t0) > P.timeout_ns) verdict = 2;
                 }
                 verdict = __shfl_sync(0xffffffffu, verdict, 0);
@@ -622,133 +727,181 @@ struct Consumer {
         return true;
     }
 
-    __device__ __forceinline__ void attn_pos(const uint2 kq, const uint2 vq) {
+    // One phase of one layer: wait for its input vector, then consume this
+    // CTA's tiles.  Phase-local state (attention accumulators, LM best) lives
+    // only inside this call.
+    template <int KIND>
+    __device__ __forceinline__ bool run(int phase, int l) {
+        if (!begin<KIND>(phase, l)) return false;
+        if (KIND == 1) {
+            AttnState a;
+            const float* qn = sm<float>(SM_QN);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a.q0[i] = qn[4 * lane + i] * P.attn_scale;
+                a.q1[i] = qn[D + 4 * lane + i] * P.attn_scale;
+                a.a0[i] = 0.f;
+                a.a1[i] = 0.f;
+            }
+            a.m0 = a.m1 = -INFINITY;
+            a.l0 = a.l1 = 0.f;
+            for_tiles(P, S, PH_ATTN, l,
+                      [&](int r, int nr, const char*, int b1, const char*, int) { tile<1>(PH_ATTN, l, r, nr, b1, &a, nullptr); });
+            end_attn(a, l);
+            return true;
+        }
+        if (KIND == 2) {
+            LmBest best{-INFINITY, 0x7fffffff};
+            for_tiles(P, S, PH_LM, l,
+                      [&](int r, int nr, const char*, int b1, const char*, int) { tile<2>(PH_LM, l, r, nr, b1, nullptr, &best); });
+            end_lm(best);
+            return true;
+        }
+        for_tiles(P, S, phase, l,
+                  [&](int r, int nr, const char*, int b1, const char*, int) { tile<KIND>(phase, l, r, nr, b1, nullptr, nullptr); });
+        return true;
+    }
+
+    __device__ __forceinline__ void attn_pos(AttnState& a, const uint2 kq, const uint2 vq) {
         float k0 = bf16lo(kq.x), k1 = bf16hi(kq.x), k2 = bf16lo(kq.y), k3 = bf16hi(kq.y);
-        float s0 = q0[0] * k0 + q0[1] * k1 + q0[2] * k2 + q0[3] * k3;
-        float s1 = q1[0] * k0 + q1[1] * k1 + q1[2] * k2 + q1[3] * k3;
+        float s0 = a.q0[0] * k0 + a.q0[1] * k1 + a.q0[2] * k2 + a.q0[3] * k3;
+        float s1 = a.q1[0] * k0 + a.q1[1] * k1 + a.q1[2] * k2 + a.q1[3] * k3;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
             s0 += __shfl_xor_sync(0xffffffffu, s0, o);
             s1 += __shfl_xor_sync(0xffffffffu, s1, o);
         }
         float v0 = bf16lo(vq.x), v1 = bf16hi(vq.x), v2 = bf16lo(vq.y), v3 = bf16hi(vq.y);
-        float n0 = fmaxf(m0, s0), c0 = expf(m0 - n0), p0 = expf(s0 - n0);
-        float n1 = fmaxf(m1, s1), c1 = expf(m1 - n1), p1 = expf(s1 - n1);
-        l0 = l0 * c0 + p0;
-        l1 = l1 * c1 + p1;
-        a0[0] = a0[0] * c0 + p0 * v0; a0[1] = a0[1] * c0 + p0 * v1; a0[2] = a0[2] * c0 + p0 * v2; a0[3] = a0[3] * c0 + p0 * v3;
-        a1[0] = a1[0] * c1 + p1 * v0; a1[1] = a1[1] * c1 + p1 * v1; a1[2] = a1[2] * c1 + p1 * v2; a1[3] = a1[3] * c1 + p1 * v3;
-        m0 = n0;
-        m1 = n1;
+        float n0 = fmaxf(a.m0, s0), c0 = expf(a.m0 - n0), p0 = expf(s0 - n0);
+        float n1 = fmaxf(a.m1, s1), c1 = expf(a.m1 - n1), p1 = expf(s1 - n1);
+        a.l0 = a.l0 * c0 + p0;
+        a.l1 = a.l1 * c1 + p1;
+        a.a0[0] = a.a0[0] * c0 + p0 * v0; a.a0[1] = a.a0[1] * c0 + p0 * v1; a.a0[2] = a.a0[2] * c0 + p0 * v2; a.a0[3] = a.a0[3] * c0 + p0 * v3;
+        a.a1[0] = a.a1[0] * c1 + p1 * v0; a.a1[1] = a.a1[1] * c1 + p1 * v1; a.a1[2] = a.a1[2] * c1 + p1 * v2; a.a1[3] = a.a1[3] * c1 + p1 * v3;
+        a.m0 = n0;
+        a.m1 = n1;
     }
 
-    __device__ void tile(int phase, int l, int r0, int nrows, const char*, int b1, const char*, int) {
+    template <int KIND>
+    __device__ __forceinline__ void tile(int phase, int l, int r0, int nrows, int b1, AttnState* a, LmBest* bst) {
         const uint32_t s = n % NSTAGES, par = (n / NSTAGES) & 1u;
+        const bool tr = P.trace && ct == 0 && n < 320;
+        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 513 + 4 * n] = globaltimer_ns();
         ++n;
-        if (!wait_full(s, par, phase, l)) return;
-        const uint8_t* st = smem + SM_STAGES + s * STAGE_BYTES;
-        const uint32_t tag = tag_of(S, l);
-        if (phase == PH_ATTN) {
-            const uint8_t* kb = st;
-            const uint8_t* vb = st + b1;
-            for (int t = warp; t < nrows; t += NCW) {
-                uint2 kq = *reinterpret_cast<const uint2*>(kb + t * D * 2 + lane * 8);
-                uint2 vq = *reinterpret_cast<const uint2*>(vb + t * D * 2 + lane * 8);
-                attn_pos(kq, vq);
+        const bool got = wait_full(s, par, phase, l);
+        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 514 + 4 * (n - 1)] = globaltimer_ns();
+        const uint8_t* st = g_smem + SM_STAGES + s * STAGE_BYTES;
+        if (KIND == 1) {
+            if (got) {
+                const uint8_t* kb = st;
+                const uint8_t* vb = st + b1;
+                for (int t = warp; t < nrows; t += NCW) {
+                    uint2 kq = *reinterpret_cast<const uint2*>(kb + t * D * 2 + lane * 8);
+                    uint2 vq = *reinterpret_cast<const uint2*>(vb + t * D * 2 + lane * 8);
+                    attn_pos(*a, kq, vq);
+                }
+                release(s);
             }
-        } else if (warp < nrows) {
+        } else {
+            mv_tile<KIND>(phase, l, r0, nrows, st, s, got, bst, n - 1);
+        }
+        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 515 + 4 * (n - 1)] = globaltimer_ns();
+    }
+
+    __device__ __forceinline__ void release(uint32_t s) {
+        __syncwarp();
+        if (lane == 0) {
+            if (P.arrive_relaxed) mbar_arrive_relaxed(&empty()[s]);
+            else mbar_arrive(&empty()[s]);
+        }
+    }
+
+    // Matrix-vector product of one staged tile (rows of length K, bf16) with
+    // the fp32 input vector X: one warp per row (GU: one warp per gate/up
+    // pair), 16-byte chunks strided over the lanes, one shuffle reduction.
+    template <int KIND>
+    __device__ __forceinline__ void mv_tile(int phase, int l, int r0, int nrows, const uint8_t* st, uint32_t s,
+                                            bool got, LmBest* bst, uint32_t) {
+        if (!got) return;
+        if (warp < nrows) {
             const int r = r0 + warp;
-            if (phase == PH_QKV || phase == PH_LM || phase == PH_GU) {
+            const uint32_t tag = tag_of(S, l);
+            if (KIND == 0 || KIND == 2) {
                 const uint4* w = reinterpret_cast<const uint4*>(st + warp * H * 2);
-                float acc = 0.f;
+                float acc = 0.f, up = 0.f;
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
-                    uint4 q = w[lane + 32 * u];
-                    const float* x = xr + 8 * u;
-                    acc += dot8(q, make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]));
+                    const int c = lane + 32 * u;
+                    const float4 lo = *reinterpret_cast<const float4*>(sx() + c * 4);
+                    const float4 hi = *reinterpret_cast<const float4*>(sx() + H / 2 + c * 4);
+                    acc += dot8(w[c], lo, hi);
+                    if (KIND == 0 && phase == PH_GU)
+                        up += dot8(reinterpret_cast<const uint4*>(st + (nrows + warp) * H * 2)[c], lo, hi);
                 }
-                if (phase == PH_GU) {
-                    const uint4* wu = reinterpret_cast<const uint4*>(st + b1 + warp * H * 2);
-                    float up = 0.f;
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        uint4 q = wu[lane + 32 * u];
-                        const float* x = xr + 8 * u;
-                        up += dot8(q, make_float4(x[0], x[1], x[2], x[3]), make_float4(x[4], x[5], x[6], x[7]));
-                    }
-                    acc = warp_sum(acc);
+                acc = warp_sum(acc);
+                if (KIND == 0 && phase == PH_GU) {
                     up = warp_sum(up);
-                    if (lane == 0) {
-                        float act = acc / (1.0f + expf(-acc)) * up;
-                        st_relaxed_u64(ll_act(P, l) + r, ll_word(act, tag));
-                    }
-                } else {
-                    acc = warp_sum(acc);
-                    if (phase == PH_QKV) {
-                        bool skip = (S.c == P.inject_skip_cta - 1) && l == 0;
-                        if (lane == 0 && !skip) st_relaxed_u64(ll_qkv(P, l) + r, ll_word(acc, tag));
-                    } else {
-                        if (lane == 0) {
-                            if (P.logits) P.logits[r] = acc;
-                            if (acc > best_v || (acc == best_v && r < best_i)) { best_v = acc; best_i = r; }
-                        }
-                    }
+                    if (lane == 0) ll_store(ll_act(P, l) + r, ll_word(acc / (1.0f + expf(-acc)) * up, tag));
+                } else if (KIND == 0) {
+                    const bool skip = (S.c == P.inject_skip_cta - 1) && l == 0;
+                    if (lane == 0 && !skip) ll_store(ll_qkv(P, l) + r, ll_word(acc, tag));
+                } else if (lane == 0) {
+                    if (P.logits) P.logits[r] = acc;
+                    if (acc > bst->v || (acc == bst->v && r < bst->i)) { bst->v = acc; bst->i = r; }
                 }
             } else {
-                // O (K=2048) and down (K=3072): x from planar shared memory.
+                // O (K=2048) and down (K=3072)
                 const int K = (phase == PH_O) ? QS : I;
                 const int CPL = K / 256;  // 16-byte chunks per lane
                 const uint4* w = reinterpret_cast<const uint4*>(st + warp * K * 2);
                 float acc = 0.f;
 #pragma unroll 4
                 for (int u = 0; u < CPL; ++u) {
-                    int c = lane + 32 * u;
-                    float4 lo = *reinterpret_cast<const float4*>(sx + c * 4);
-                    float4 hi = *reinterpret_cast<const float4*>(sx + K / 2 + c * 4);
-                    acc += dot8(w[c], lo, hi);
+                    const int c = lane + 32 * u;
+                    acc += dot8(w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
+                                *reinterpret_cast<const float4*>(sx() + K / 2 + c * 4));
                 }
                 acc = warp_sum(acc);
                 if (lane == 0) {
-                    if (phase == PH_O) st_relaxed_u64(ll_hmid(P, l) + r, ll_word(acc + sh[r], tag));
-                    else st_relaxed_u64(ll_hout(P, l) + r, ll_word(acc + sh2[r], tag));
+                    if (phase == PH_O) ll_store(ll_hmid(P, l) + r, ll_word(acc + sh()[r], tag));
+                    else ll_store(ll_hout(P, l) + r, ll_word(acc + sh2()[r], tag));
                 }
             }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        release(s);
     }
 
-    __device__ void end_attn(int l) {
-        float* acc = reinterpret_cast<float*>(smem + SM_ACC);   // [16][2][128]
-        float* ml = reinterpret_cast<float*>(smem + SM_ML);     // [16][2][2]
+    __device__ __forceinline__ void end_attn(AttnState& a, int l) {
+        float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);   // [16][2][128]
+        float* ml = reinterpret_cast<float*>(g_smem + SM_ML);     // [16][2][2]
         if (ok && S.last && warp == 0) {
             // the current position, from the bf16-rounded values in shared memory
-            const float* kp = reinterpret_cast<const float*>(smem + SM_KP);
-            const float* vp = reinterpret_cast<const float*>(smem + SM_VP);
+            const float* kp = reinterpret_cast<const float*>(g_smem + SM_KP);
+            const float* vp = reinterpret_cast<const float*>(g_smem + SM_VP);
             float k0 = kp[4 * lane], k1 = kp[4 * lane + 1], k2 = kp[4 * lane + 2], k3 = kp[4 * lane + 3];
-            float s0 = q0[0] * k0 + q0[1] * k1 + q0[2] * k2 + q0[3] * k3;
-            float s1 = q1[0] * k0 + q1[1] * k1 + q1[2] * k2 + q1[3] * k3;
+            float s0 = a.q0[0] * k0 + a.q0[1] * k1 + a.q0[2] * k2 + a.q0[3] * k3;
+            float s1 = a.q1[0] * k0 + a.q1[1] * k1 + a.q1[2] * k2 + a.q1[3] * k3;
             s0 = warp_sum(s0);
             s1 = warp_sum(s1);
-            float n0 = fmaxf(m0, s0), c0 = expf(m0 - n0), p0 = expf(s0 - n0);
-            float n1 = fmaxf(m1, s1), c1 = expf(m1 - n1), p1 = expf(s1 - n1);
-            l0 = l0 * c0 + p0;
-            l1 = l1 * c1 + p1;
+            float n0 = fmaxf(a.m0, s0), c0 = expf(a.m0 - n0), p0 = expf(s0 - n0);
+            float n1 = fmaxf(a.m1, s1), c1 = expf(a.m1 - n1), p1 = expf(s1 - n1);
+            a.l0 = a.l0 * c0 + p0;
+            a.l1 = a.l1 * c1 + p1;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float vv = vp[4 * lane + i];
-                a0[i] = a0[i] * c0 + p0 * vv;
-                a1[i] = a1[i] * c1 + p1 * vv;
+                a.a0[i] = a.a0[i] * c0 + p0 * vv;
+                a.a1[i] = a.a1[i] * c1 + p1 * vv;
             }
-            m0 = n0;
-            m1 = n1;
+            a.m0 = n0;
+            a.m1 = n1;
         }
         if (lane == 0) {
-            ml[warp * 4 + 0] = m0; ml[warp * 4 + 1] = l0;
-            ml[warp * 4 + 2] = m1; ml[warp * 4 + 3] = l1;
+            ml[warp * 4 + 0] = a.m0; ml[warp * 4 + 1] = a.l0;
+            ml[warp * 4 + 2] = a.m1; ml[warp * 4 + 3] = a.l1;
         }
-        *reinterpret_cast<float4*>(acc + (warp * 2 + 0) * D + 4 * lane) = make_float4(a0[0], a0[1], a0[2], a0[3]);
-        *reinterpret_cast<float4*>(acc + (warp * 2 + 1) * D + 4 * lane) = make_float4(a1[0], a1[1], a1[2], a1[3]);
+        *reinterpret_cast<float4*>(acc + (warp * 2 + 0) * D + 4 * lane) = make_float4(a.a0[0], a.a0[1], a.a0[2], a.a0[3]);
+        *reinterpret_cast<float4*>(acc + (warp * 2 + 1) * D + 4 * lane) = make_float4(a.a1[0], a.a1[1], a.a1[2], a.a1[3]);
         named_bar_sync(BAR_CONSUMERS, NCT);
         float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
         const int h = warp;  // warps 0 and 1 combine heads 0 and 1
@@ -767,12 +920,12 @@ struct Consumer {
             if (warp < 2 && ok) {
                 float inv = 1.0f / Ls;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) st_relaxed_u64(out + h * D + 4 * lane + i, ll_word(A[i] * inv, tag));
+                for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(A[i] * inv, tag));
             }
             return;
         }
         // split-K: publish the partial, the last unit of this kv head combines
-        volatile int* f = flags;
+        volatile int* f = flags();
         if (warp < 2) {
             float* pp = part_of(P, S.ug, S.uj, h);
             if (lane == 0) { pp[0] = M; pp[1] = Ls; }
@@ -804,14 +957,22 @@ struct Consumer {
             }
             float inv = 1.0f / gl;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) st_relaxed_u64(out + h * D + 4 * lane + i, ll_word(G4[i] * inv, tag));
+            for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(G4[i] * inv, tag));
         }
     }
 
-    __device__ void end_lm() {
-        float* bv = reinterpret_cast<float*>(smem + SM_BEST);
-        int* bi = reinterpret_cast<int*>(smem + SM_BEST) + NCW;
-        if (lane == 0) { bv[warp] = best_v; bi[warp] = best_i; }
+    __device__ __forceinline__ void end_lm(const LmBest& best) {
+        float* bv = reinterpret_cast<float*>(g_smem + SM_BEST);
+        int* bi = reinterpret_cast<int*>(g_smem + SM_BEST) + NCW;
+        float v = best.v;
+        int i = best.i;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float ov = __shfl_xor_sync(0xffffffffu, v, o);
+            int oi = __shfl_xor_sync(0xffffffffu, i, o);
+            if (ov > v || (ov == v && oi < i)) { v = ov; i = oi; }
+        }
+        if (lane == 0) { bv[warp] = v; bi[warp] = i; }
         if (!agree()) return;
         if (ct == 0) {
             float v = bv[0];
@@ -841,33 +1002,59 @@ struct Consumer {
     }
 };
 
-__global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_constant__ KParams P) {
-    extern __shared__ __align__(1024) uint8_t smem[];
-    Control* C = ctrl_of(P);
-    volatile int* flags = reinterpret_cast<volatile int*>(smem + SM_FLAGS);
+// Consumer progress between phase calls: tiles consumed (bits 0-23), block-sum
+// parity (bit 24), this thread failed (bit 25), stop the walk (bit 26).
+template <int KIND>
+__device__ __noinline__ uint32_t consumer_phase(const KParams* P, int phase, int l, uint32_t st) {
+    Consumer c(*P, *sm<Sched>(SM_SCHED));
+    c.n = st & 0xffffffu;
+    c.red_par = (st >> 24) & 1u;
+    c.ok = ((st >> 25) & 1u) == 0;
+    const bool go = c.template run<KIND>(phase, l);
+    return (c.n & 0xffffffu) | ((uint32_t)c.red_par << 24) | (c.ok ? 0u : (1u << 25)) | (go ? 0u : (1u << 26));
+}
 
-    Sched S;
-    S.G = gridDim.x;
-    S.c = blockIdx.x;
+// Walk visitor for the consumer warps: each phase kind is its own function so
+// the register allocator sees one phase at a time (no spills).
+struct ConsumerWalk {
+    const KParams* P;
+    uint32_t st = 0;
+    __device__ bool run(int phase, int l) {
+        if (phase == PH_ATTN) st = consumer_phase<1>(P, phase, l, st);
+        else if (phase == PH_LM) st = consumer_phase<2>(P, phase, l, st);
+        else if (phase == PH_O || phase == PH_DOWN) st = consumer_phase<3>(P, phase, l, st);
+        else st = consumer_phase<0>(P, phase, l, st);
+        return (st & (1u << 26)) == 0;
+    }
+};
+
+__global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_constant__ KParams P) {
+    Control* C = ctrl_of(P);
+    volatile int* flags = sm<volatile int>(SM_FLAGS);
     const int pos = P.position_ptr ? *P.position_ptr : P.position;
     const int tok = P.input_token_ptr ? *P.input_token_ptr : P.input_token;
     if (pos < 0 || pos >= P.max_seq_len) {
-        if (S.c == 0 && threadIdx.x == 0) record_error(P, MQ_ERR_BAD_POSITION, (uint32_t)pos);
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_error(P, MQ_ERR_BAD_POSITION, (uint32_t)pos);
         return;
     }
     if (tok < 0 || tok >= V) {
-        if (S.c == 0 && threadIdx.x == 0) record_error(P, MQ_ERR_BAD_TOKEN, (uint32_t)tok);
+        if (blockIdx.x == 0 && threadIdx.x == 0) record_error(P, MQ_ERR_BAD_TOKEN, (uint32_t)tok);
         return;
     }
-    S.pos = pos;
-    S.L = pos + 1;
-    S.tag_base = (int)((C->epoch + 1u) << 6);
-    S.qkv_a = split_at(QKV, S.G, S.c); S.qkv_b = split_at(QKV, S.G, S.c + 1);
-    S.o_a = split_at(H, S.G, S.c);     S.o_b = split_at(H, S.G, S.c + 1);
-    S.gu_a = split_at(I, S.G, S.c);    S.gu_b = split_at(I, S.G, S.c + 1);
-    S.dn_a = S.o_a;                    S.dn_b = S.o_b;
-    S.lm_a = split_at(V, S.G, S.c);    S.lm_b = split_at(V, S.G, S.c + 1);
-    {
+
+    // The CTA's slice of every phase lives in shared memory (not registers).
+    Sched& S = *sm<Sched>(SM_SCHED);
+    if (threadIdx.x == 0) {
+        S.G = gridDim.x;
+        S.c = blockIdx.x;
+        S.pos = pos;
+        S.L = pos + 1;
+        S.tag_base = (int)((C->epoch + 1u) << 6);
+        S.qkv_a = split_at(QKV, S.G, S.c); S.qkv_b = split_at(QKV, S.G, S.c + 1);
+        S.o_a = split_at(H, S.G, S.c);     S.o_b = split_at(H, S.G, S.c + 1);
+        S.gu_a = split_at(I, S.G, S.c);    S.gu_b = split_at(I, S.G, S.c + 1);
+        S.dn_a = S.o_a;                    S.dn_b = S.o_b;
+        S.lm_a = split_at(V, S.G, S.c);    S.lm_b = split_at(V, S.G, S.c + 1);
         const int chunk = P.attn_chunk > 0 ? P.attn_chunk : 64;
         int C_ = (S.L + chunk - 1) / chunk;
         C_ = min(C_, S.G / NKV);
@@ -883,11 +1070,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_c
         S.last = (S.uj == C_ - 1);
         S.kv_s = ps;
         S.kv_e = S.last ? pe - 1 : pe;   // the current position comes from registers, not the cache
-    }
 
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + SM_BARS);
-    uint64_t* empty = full + NSTAGES;
-    if (threadIdx.x == 0) {
+        uint64_t* full = sm<uint64_t>(SM_BARS);
+        uint64_t* empty = full + NSTAGES;
         for (int s = 0; s < NSTAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], NCW);
@@ -897,18 +1082,28 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_c
         flags[1] = tok;
         flags[2] = 0;
     }
+    {
+        // per-layer pointer table -> shared memory (read at every phase start)
+        const uint64_t* src = reinterpret_cast<const uint64_t*>(P.layers);
+        uint64_t* dst = sm<uint64_t>(SM_LAYERS);
+        const int words = P.num_layers * (int)(sizeof(LDGLayerWeights) / 8);
+        for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    }
     __syncthreads();
 
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) {
-            Producer pr(P, smem);
+            Producer pr(P, g_smem);
             walk(P, S, pr);
+            if (P.trace) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 502] = globaltimer_ns();
             pr.drain();
         }
         return;
     }
-    Consumer cs(P, S, smem);
+    ConsumerWalk cs{&P};
+    if (P.trace && threadIdx.x == 32) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 500] = globaltimer_ns();
     walk(P, S, cs);
+    if (P.trace && threadIdx.x == 32) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 501] = globaltimer_ns();
 }
 
 }  // namespace mq
@@ -920,6 +1115,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_c
 namespace {
 
 thread_local int g_last_error = MQ_OK;
+thread_local char g_detail[256] = "";
+
+// Record which CUDA call failed and why; returns MQ_ERR_CUDA.
+int cuda_fail(cudaError_t e, const char* what) {
+    snprintf(g_detail, sizeof(g_detail), "%s: %s", what, cudaGetErrorString(e));
+    return MQ_ERR_CUDA;
+}
+
+int note(int code, const char* what) {
+    snprintf(g_detail, sizeof(g_detail), "%s", what);
+    return code;
+}
 
 struct DeviceWorkspace {
     void* ptr = nullptr;
@@ -938,7 +1145,7 @@ int configure_kernel(int dev) {
     if (dev >= 0 && dev < 64 && kernel_configured[dev]) return MQ_OK;
     cudaError_t e = cudaFuncSetAttribute(mq::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          mq::SMEM_BYTES);
-    if (e != cudaSuccess) return MQ_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
     if (dev >= 0 && dev < 64) kernel_configured[dev] = true;
     return MQ_OK;
 }
@@ -972,15 +1179,16 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     if (!p->input_token_ptr && (p->input_token < 0 || p->input_token >= MQ_VOCAB_SIZE))
         return MQ_ERR_INVALID_ARGUMENT;
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess) return MQ_ERR_CUDA;
+    cudaError_t ce = cudaGetDevice(&dev);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
     int rc = configure_kernel(dev);
     if (rc) return rc;
     int G = p->num_ctas > 0 ? p->num_ctas : default_ctas(dev);
     if (G < mq::NKV || G > mq::MAX_CTAS) return MQ_ERR_INVALID_ARGUMENT;
     int maxb = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel, mq::NTHREADS, mq::SMEM_BYTES) !=
-            cudaSuccess || maxb < 1)
-        return MQ_ERR_CUDA;
+    ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel, mq::NTHREADS, mq::SMEM_BYTES);
+    if (ce != cudaSuccess) return cuda_fail(ce, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+    if (maxb < 1) return note(MQ_ERR_CUDA, "decode kernel does not fit on one SM (occupancy 0)");
     mq::KParams k;
     k.input_token = p->input_token;
     k.input_token_ptr = p->input_token_ptr;
@@ -1005,6 +1213,20 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     k.attn_chunk = p->attn_chunk;
     k.timeout_ns = p->timeout_ns > 0 ? p->timeout_ns : 2000000000ll;
     k.inject_skip_cta = p->inject_skip_cta;
+    k.trace = p->trace;
+    {
+        // experiment hooks (handoff polling strategy)
+        const char* e = getenv("MQ_POLL_MODE");
+        k.poll_mode = e ? atoi(e) : 2;
+        e = getenv("MQ_POLL_WARPS");
+        k.poll_warps = e ? atoi(e) : mq::NCW;
+        e = getenv("MQ_POLL_SLEEP");
+        k.poll_sleep_ns = e ? atoi(e) : 0;
+        e = getenv("MQ_STORE_MODE");
+        k.store_mode = e ? atoi(e) : 0;
+        e = getenv("MQ_ARRIVE_RELAXED");
+        k.arrive_relaxed = e ? atoi(e) : 1;
+    }
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
@@ -1017,7 +1239,7 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t e = cudaLaunchKernelEx(&cfg, mq::decode_step_kernel, k);
-    if (e != cudaSuccess) return MQ_ERR_CUDA;
+    if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(decode_step_kernel, cooperative)");
     return MQ_OK;
 }
 
@@ -1108,8 +1330,10 @@ int mq_decode_fetch(const void* workspace, int* token, uint32_t* error, uint32_t
     if (!workspace) return MQ_ERR_WORKSPACE;
     static thread_local uint32_t* pinned = nullptr;
     if (!pinned && cudaHostAlloc((void**)&pinned, 64, cudaHostAllocDefault) != cudaSuccess) return MQ_ERR_CUDA;
-    if (cudaMemcpyAsync(pinned, workspace, 32, cudaMemcpyDeviceToHost, stream) != cudaSuccess) return MQ_ERR_CUDA;
-    if (cudaStreamSynchronize(stream) != cudaSuccess) return MQ_ERR_CUDA;
+    cudaError_t e = cudaMemcpyAsync(pinned, workspace, 32, cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(result)");
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
     const mq::Control* c = reinterpret_cast<const mq::Control*>(pinned);
     if (token) *token = c->last_token;
     if (error) *error = c->error;
@@ -1124,6 +1348,8 @@ int mq_decode_default_ctas(void) {
 }
 
 int mq_get_last_error(void) { return g_last_error; }
+
+const char* mq_last_error_detail(void) { return g_detail; }
 
 const char* mq_error_string(int code) {
     switch (code) {

@@ -85,7 +85,7 @@ torch::Tensor layer_table(const std::vector<LDGLayerWeights>& host, const torch:
                                  char b[16];
                                  snprintf(b, sizeof(b), "%x", info);
                                  return std::string(b);
-                             }() + ")");
+                             }() + ")" + (code == MQ_ERR_CUDA ? std::string(" ") + mq_last_error_detail() : ""));
 }
 
 // ---------------------------------------------------------------------------
@@ -194,6 +194,8 @@ public:
     void set_attn_chunk(int n) { attn_chunk_ = n; }
     void set_timeout_ns(long long t) { timeout_ns_ = t; }
     void set_inject_skip_cta(int c) { inject_skip_cta_ = c; }
+    // Profiling: device int64 buffer of num_ctas * 512 timestamps, or 0 to disable.
+    void set_trace(int64_t ptr) { trace_ = reinterpret_cast<unsigned long long*>(ptr); }
     int num_ctas() const { return num_ctas_ > 0 ? num_ctas_ : mq_decode_default_ctas(); }
 
     // Raw decode step for benchmarks: token from a device pointer (feedback),
@@ -242,6 +244,7 @@ protected:
         p.attn_chunk = attn_chunk_;
         p.timeout_ns = timeout_ns_;
         p.inject_skip_cta = inject_skip_cta_;
+        p.trace = trace_;
         return p;
     }
 
@@ -280,6 +283,7 @@ protected:
     int attn_chunk_ = 0;
     long long timeout_ns_ = 0;
     int inject_skip_cta_ = 0;
+    unsigned long long* trace_ = nullptr;
     torch::Device device_{torch::kCUDA, 0};
     torch::Tensor embed_, final_norm_, lm_head_, cos_, sin_, d_layers_;
     std::vector<torch::Tensor> layer_tensors_;
@@ -476,7 +480,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("num_ctas", &MegakernelDecoder::num_ctas)
         .def("set_attn_chunk", &MegakernelDecoder::set_attn_chunk)
         .def("set_timeout_ns", &MegakernelDecoder::set_timeout_ns)
-        .def("set_inject_skip_cta", &MegakernelDecoder::set_inject_skip_cta);
+        .def("set_inject_skip_cta", &MegakernelDecoder::set_inject_skip_cta)
+        .def("set_trace", &MegakernelDecoder::set_trace);
     py::class_<MegakernelPrefillDecoder, MegakernelDecoder>(m, "MegakernelPrefillDecoder")
         .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
                       torch::Tensor, int, int, int>(),
