@@ -142,6 +142,25 @@ int mq_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream)
 /* Launch one decode step.  Host-side argument checks return an error code
  * without launching; device-side failures land in the workspace error word. */
 int mq_decode(const mq_decode_params* params, cudaStream_t stream);
+
+/* mq_decode_noalloc: the same decode step for callers that must not allocate
+ * device memory -- for example code running under an allocator or memory
+ * pool that owns all device memory, or a runtime whose own workspace budget is
+ * fixed up front and cannot grant the few hundred KB mq_decode needs.  It has
+ * no counterpart in the reference.  The inter-CTA scratch lives in a static
+ * device array of MQ_NOALLOC_SCRATCH_BYTES bytes (held on every GPU that loads
+ * this library, until the process exits); params->workspace and
+ * workspace_bytes are ignored.  The caller still passes every input and output
+ * buffer.  The first call on a device resolves the array's address and clears
+ * it, so make that first call before any stream capture.  Every call on a
+ * device shares the array, so calls that overlap on the GPU (different
+ * streams, or other threads) race.  num_ctas above 256 or num_layers above 63
+ * are rejected with MQ_ERR_INVALID_ARGUMENT.  A device-side wait failure
+ * leaves the output token unwritten; the scratch then holds a stale error and
+ * the process should stop using this entry point on that device.  Calls no
+ * cudaMalloc, cudaFree or other allocating routine. */
+#define MQ_NOALLOC_SCRATCH_BYTES 450816
+int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream);
 /* Copy the workspace error word (and the auxiliary info word) to the host;
  * synchronises `stream`. */
 int mq_decode_read_error(const void* workspace, uint32_t* error, uint32_t* info, cudaStream_t stream);

@@ -1316,6 +1316,54 @@ int mq_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream)
 
 int mq_decode(const mq_decode_params* params, cudaStream_t stream) { return launch(params, stream); }
 
+}  // extern "C"
+
+// ---- decode without any allocation -------------------------------------------
+// Scratch for mq_decode_noalloc: one workspace's worth (MQ_NOALLOC_SCRATCH_BYTES)
+// in a file-scope device array.  Every GPU that loads this library holds it
+// until the process exits.  In host code the symbol is only a stand-in; the
+// device address comes from cudaGetSymbolAddress, taken once per device.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[mq::WS_BYTES];
+static_assert(mq::WS_BYTES == MQ_NOALLOC_SCRATCH_BYTES, "header states the static scratch size");
+
+namespace {
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[64] = {nullptr};
+}  // namespace
+
+extern "C" {
+
+int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream) {
+    if (!params) return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: params is NULL");
+    if (params->num_ctas > mq::MAX_CTAS)
+        return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: num_ctas exceeds the 256 CTAs the static scratch holds");
+    if (params->num_layers > MQ_MAX_LAYERS)
+        return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: num_layers exceeds the 63 layers the static scratch holds");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    if (dev < 0 || dev >= 64) return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: device index above 63");
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+        if (!g_noalloc_ptr[dev]) {
+            // First call on this device (device current): resolve the array's
+            // device address and clear it.  No allocation happens.
+            void* ptr = nullptr;
+            e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_noalloc_scratch)");
+            e = cudaMemsetAsync(ptr, 0, mq::WS_BYTES, stream);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static scratch)");
+            g_noalloc_ptr[dev] = ptr;
+        }
+        scratch = g_noalloc_ptr[dev];
+    }
+    mq_decode_params p = *params;
+    p.workspace = scratch;
+    p.workspace_bytes = mq::WS_BYTES;
+    return launch(&p, stream);
+}
+
 int mq_decode_read_error(const void* workspace, uint32_t* error, uint32_t* info, cudaStream_t stream) {
     if (!workspace) return MQ_ERR_WORKSPACE;
     uint32_t h[3] = {0, 0, 0};
