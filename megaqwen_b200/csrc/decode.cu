@@ -74,6 +74,12 @@ constexpr int GU_TILE = cmin(NCW, STAGE_BYTES / (2 * H * 2));   // 8 gate+up row
 constexpr int DOWN_TILE = cmin(NCW, STAGE_BYTES / (I * 2));     // 5 rows
 constexpr int LM_TILE = cmin(NCW, STAGE_BYTES / (H * 2));       // 15 rows
 constexpr int HPT = (H + NCT - 1) / NCT;             // hidden elements per consumer thread (3)
+constexpr int MV_GROUP = 3;                          // ring stages consumed together by a matvec phase
+constexpr int MV_Q = 3;                              // rows per warp in a group
+static_assert(MV_GROUP * QKV_TILE <= MV_Q * NCW && MV_GROUP * LM_TILE <= MV_Q * NCW &&
+              MV_GROUP * GU_TILE <= MV_Q * NCW && MV_GROUP * O_TILE <= MV_Q * NCW &&
+              MV_GROUP * DOWN_TILE <= MV_Q * NCW, "a group's rows fit MV_Q rows per warp");
+static_assert(MV_GROUP < NSTAGES, "the producer can fill a whole group");
 constexpr int KV_TILE = STAGE_BYTES / (2 * D * 2);   // 64 positions (K and V)
 static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <= NCW && LM_TILE <= NCW,
               "one consumer warp per row of a tile");
@@ -230,6 +236,12 @@ __device__ __forceinline__ float dot8(uint4 w, float4 lo, float4 hi) {
     return s;
 }
 
+__device__ __forceinline__ const char* qkv_row(const LDGLayerWeights& W, int r) {
+    if (r < QS) return (const char*)W.q_proj_weight + (size_t)r * H * 2;
+    if (r < QS + KVS) return (const char*)W.k_proj_weight + (size_t)(r - QS) * H * 2;
+    return (const char*)W.v_proj_weight + (size_t)(r - QS - KVS) * H * 2;
+}
+
 // ---- the per-CTA tile lists, shared by producer and consumers ------------------
 // for_tiles calls f(first_row, rows, src1, bytes1, src2, bytes2) for every
 // stage-sized tile this CTA owns in one phase of one layer, in ring order.
@@ -245,15 +257,13 @@ __device__ __forceinline__ void for_tiles(const KParams& P, const Sched& S, int 
     }
     const LDGLayerWeights& W = sm<LDGLayerWeights>(SM_LAYERS)[l];
     if (phase == PH_QKV) {
-        for (int r = S.qkv_a; r < S.qkv_b;) {
-            const char* base;
-            int r0, lim;
-            if (r < QS) { base = (const char*)W.q_proj_weight; r0 = r; lim = QS; }
-            else if (r < QS + KVS) { base = (const char*)W.k_proj_weight; r0 = r - QS; lim = QS + KVS; }
-            else { base = (const char*)W.v_proj_weight; r0 = r - QS - KVS; lim = QKV; }
-            int n = min(min(S.qkv_b, lim) - r, QKV_TILE);
-            f(r, n, base + (size_t)r0 * H * 2, n * H * 2, (const char*)nullptr, 0);
-            r += n;
+        // Rows of the concatenated [q; k; v] space in tiles of QKV_TILE; a tile
+        // that crosses a matrix boundary is two bulk copies into one stage.
+        for (int r = S.qkv_a; r < S.qkv_b; r += QKV_TILE) {
+            const int e = min(S.qkv_b, r + QKV_TILE);
+            const int cut = (r < QS && e > QS) ? QS : ((r < QS + KVS && e > QS + KVS) ? QS + KVS : e);
+            f(r, e - r, qkv_row(W, r), (cut - r) * H * 2, cut < e ? qkv_row(W, cut) : (const char*)nullptr,
+              (e - cut) * H * 2);
         }
     } else if (phase == PH_ATTN) {
         for (int t = S.kv_s; t < S.kv_e; t += KV_TILE) {
@@ -750,16 +760,120 @@ struct Consumer {
             end_attn(a, l);
             return true;
         }
+        float xr[32];  // K=1024 phases: this lane's input chunks lane + 32u, read once per phase
+        if (KIND == 0 || KIND == 2) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int c = lane + 32 * u;
+                const float4 lo = *reinterpret_cast<const float4*>(sx() + c * 4);
+                const float4 hi = *reinterpret_cast<const float4*>(sx() + H / 2 + c * 4);
+                xr[8 * u + 0] = lo.x; xr[8 * u + 1] = lo.y; xr[8 * u + 2] = lo.z; xr[8 * u + 3] = lo.w;
+                xr[8 * u + 4] = hi.x; xr[8 * u + 5] = hi.y; xr[8 * u + 6] = hi.z; xr[8 * u + 7] = hi.w;
+            }
+        }
         if (KIND == 2) {
             LmBest best{-INFINITY, 0x7fffffff};
-            for_tiles(P, S, PH_LM, l,
-                      [&](int r, int nr, const char*, int b1, const char*, int) { tile<2>(PH_LM, l, r, nr, b1, nullptr, &best); });
+            mv_phase<2>(PH_LM, l, xr, &best);
             end_lm(best);
             return true;
         }
-        for_tiles(P, S, phase, l,
-                  [&](int r, int nr, const char*, int b1, const char*, int) { tile<KIND>(phase, l, r, nr, b1, nullptr, nullptr); });
+        mv_phase<KIND>(phase, l, xr, nullptr);
         return true;
+    }
+
+    // Matrix-vector products of one phase.  The phase's tiles are consumed in
+    // groups of up to MV_GROUP ring stages; the group's rows are spread over
+    // the 15 warps (row j -> warp j mod 15), so each warp runs up to three
+    // independent dot-product chains at once instead of one chain per tile.
+    // One warp per row: 16-byte chunks strided over the lanes, one shuffle
+    // reduction per row.  K = 1024 inputs come from registers (xr), K = 2048 /
+    // 3072 from the planar X vector.  The tiling matches for_tiles exactly.
+    template <int KIND>
+    __device__ __forceinline__ void mv_phase(int phase, int l, const float* xr, LmBest* bst) {
+        int a, b, T;
+        if (phase == PH_QKV) { a = S.qkv_a; b = S.qkv_b; T = QKV_TILE; }
+        else if (phase == PH_GU) { a = S.gu_a; b = S.gu_b; T = GU_TILE; }
+        else if (phase == PH_O) { a = S.o_a; b = S.o_b; T = O_TILE; }
+        else if (phase == PH_DOWN) { a = S.dn_a; b = S.dn_b; T = DOWN_TILE; }
+        else { a = S.lm_a; b = S.lm_b; T = LM_TILE; }
+        const int K = (phase == PH_O) ? QS : (phase == PH_DOWN ? I : H);
+        const int R = b - a;
+        const int ntiles = (R + T - 1) / T;
+        const uint32_t tag = tag_of(S, l);
+        for (int g0 = 0; g0 < ntiles; g0 += MV_GROUP) {
+            const int g1 = min(ntiles, g0 + MV_GROUP);
+            bool got = true;
+            for (int i = g0; i < g1; ++i) {
+                const uint32_t t = n + (uint32_t)(i - g0);
+                got = wait_full(t % NSTAGES, (t / NSTAGES) & 1u, phase, l) && got;
+            }
+            const int j0 = g0 * T, j1 = min(g1 * T, R);
+            if (got) {
+                float acc[MV_Q], up[MV_Q];
+#pragma unroll
+                for (int q = 0; q < MV_Q; ++q) {
+                    acc[q] = 0.f;
+                    up[q] = 0.f;
+                    const int j = j0 + warp + NCW * q;
+                    if (j < j1) {
+                        const int ti = j / T, lr = j - ti * T;
+                        const uint8_t* st = g_smem + SM_STAGES + ((n + (uint32_t)(ti - g0)) % NSTAGES) * STAGE_BYTES;
+                        if (KIND == 0 || KIND == 2) {
+                            const uint4* w = reinterpret_cast<const uint4*>(st + lr * H * 2);
+                            const uint4* wu = reinterpret_cast<const uint4*>(st + (min(T, R - ti * T) + lr) * H * 2);
+#pragma unroll
+                            for (int u = 0; u < 4; ++u) {
+                                const int c = lane + 32 * u;
+                                const float4 lo = make_float4(xr[8 * u + 0], xr[8 * u + 1], xr[8 * u + 2], xr[8 * u + 3]);
+                                const float4 hi = make_float4(xr[8 * u + 4], xr[8 * u + 5], xr[8 * u + 6], xr[8 * u + 7]);
+                                acc[q] += dot8(w[c], lo, hi);
+                                if (KIND == 0 && phase == PH_GU) up[q] += dot8(wu[c], lo, hi);
+                            }
+                        } else {
+                            const uint4* w = reinterpret_cast<const uint4*>(st + lr * K * 2);
+                            const int CPL = K / 256;
+#pragma unroll 4
+                            for (int u = 0; u < CPL; ++u) {
+                                const int c = lane + 32 * u;
+                                acc[q] += dot8(w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
+                                               *reinterpret_cast<const float4*>(sx() + K / 2 + c * 4));
+                            }
+                        }
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                    for (int q = 0; q < MV_Q; ++q) {
+                        acc[q] += __shfl_xor_sync(0xffffffffu, acc[q], o);
+                        if (KIND == 0 && phase == PH_GU) up[q] += __shfl_xor_sync(0xffffffffu, up[q], o);
+                    }
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int q = 0; q < MV_Q; ++q) {
+                        const int j = j0 + warp + NCW * q;
+                        if (j >= j1) continue;
+                        const int r = a + j;
+                        const float v = acc[q];
+                        if (KIND == 2) {
+                            if (P.logits) P.logits[r] = v;
+                            if (v > bst->v || (v == bst->v && r < bst->i)) { bst->v = v; bst->i = r; }
+                        } else if (phase == PH_GU) {
+                            ll_store(ll_act(P, l) + r, ll_word(v / (1.0f + expf(-v)) * up[q], tag));
+                        } else if (phase == PH_QKV) {
+                            if (!((S.c == P.inject_skip_cta - 1) && l == 0)) ll_store(ll_qkv(P, l) + r, ll_word(v, tag));
+                        } else if (phase == PH_O) {
+                            ll_store(ll_hmid(P, l) + r, ll_word(v + sh()[r], tag));
+                        } else {
+                            ll_store(ll_hout(P, l) + r, ll_word(v + sh2()[r], tag));
+                        }
+                    }
+                }
+                for (int i = g0; i < g1; ++i) release((n + (uint32_t)(i - g0)) % NSTAGES);
+            }
+            n += (uint32_t)(g1 - g0);
+        }
     }
 
     __device__ __forceinline__ void attn_pos(AttnState& a, const uint2 kq, const uint2 vq) {
@@ -802,8 +916,6 @@ struct Consumer {
                 }
                 release(s);
             }
-        } else {
-            mv_tile<KIND>(phase, l, r0, nrows, st, s, got, bst, n - 1);
         }
         if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 515 + 4 * (n - 1)] = globaltimer_ns();
     }
@@ -814,61 +926,6 @@ struct Consumer {
             if (P.arrive_relaxed) mbar_arrive_relaxed(&empty()[s]);
             else mbar_arrive(&empty()[s]);
         }
-    }
-
-    // Matrix-vector product of one staged tile (rows of length K, bf16) with
-    // the fp32 input vector X: one warp per row (GU: one warp per gate/up
-    // pair), 16-byte chunks strided over the lanes, one shuffle reduction.
-    template <int KIND>
-    __device__ __forceinline__ void mv_tile(int phase, int l, int r0, int nrows, const uint8_t* st, uint32_t s,
-                                            bool got, LmBest* bst, uint32_t) {
-        if (!got) return;
-        if (warp < nrows) {
-            const int r = r0 + warp;
-            const uint32_t tag = tag_of(S, l);
-            if (KIND == 0 || KIND == 2) {
-                const uint4* w = reinterpret_cast<const uint4*>(st + warp * H * 2);
-                float acc = 0.f, up = 0.f;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int c = lane + 32 * u;
-                    const float4 lo = *reinterpret_cast<const float4*>(sx() + c * 4);
-                    const float4 hi = *reinterpret_cast<const float4*>(sx() + H / 2 + c * 4);
-                    acc += dot8(w[c], lo, hi);
-                    if (KIND == 0 && phase == PH_GU)
-                        up += dot8(reinterpret_cast<const uint4*>(st + (nrows + warp) * H * 2)[c], lo, hi);
-                }
-                acc = warp_sum(acc);
-                if (KIND == 0 && phase == PH_GU) {
-                    up = warp_sum(up);
-                    if (lane == 0) ll_store(ll_act(P, l) + r, ll_word(acc / (1.0f + expf(-acc)) * up, tag));
-                } else if (KIND == 0) {
-                    const bool skip = (S.c == P.inject_skip_cta - 1) && l == 0;
-                    if (lane == 0 && !skip) ll_store(ll_qkv(P, l) + r, ll_word(acc, tag));
-                } else if (lane == 0) {
-                    if (P.logits) P.logits[r] = acc;
-                    if (acc > bst->v || (acc == bst->v && r < bst->i)) { bst->v = acc; bst->i = r; }
-                }
-            } else {
-                // O (K=2048) and down (K=3072)
-                const int K = (phase == PH_O) ? QS : I;
-                const int CPL = K / 256;  // 16-byte chunks per lane
-                const uint4* w = reinterpret_cast<const uint4*>(st + warp * K * 2);
-                float acc = 0.f;
-#pragma unroll 4
-                for (int u = 0; u < CPL; ++u) {
-                    const int c = lane + 32 * u;
-                    acc += dot8(w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
-                                *reinterpret_cast<const float4*>(sx() + K / 2 + c * 4));
-                }
-                acc = warp_sum(acc);
-                if (lane == 0) {
-                    if (phase == PH_O) ll_store(ll_hmid(P, l) + r, ll_word(acc + sh()[r], tag));
-                    else ll_store(ll_hout(P, l) + r, ll_word(acc + sh2()[r], tag));
-                }
-            }
-        }
-        release(s);
     }
 
     __device__ __forceinline__ void end_attn(AttnState& a, int l) {
