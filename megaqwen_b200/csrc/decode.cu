@@ -773,11 +773,17 @@ struct Consumer {
         }
         if (KIND == 2) {
             LmBest best{-INFINITY, 0x7fffffff};
-            mv_phase<2>(PH_LM, l, xr, &best);
+            mv_phase<2, PH_LM>(l, xr, &best);
             end_lm(best);
             return true;
         }
-        mv_phase<KIND>(phase, l, xr, nullptr);
+        if (KIND == 0) {
+            if (phase == PH_QKV) mv_phase<0, PH_QKV>(l, xr, nullptr);
+            else mv_phase<0, PH_GU>(l, xr, nullptr);
+        } else {
+            if (phase == PH_O) mv_phase<3, PH_O>(l, xr, nullptr);
+            else mv_phase<3, PH_DOWN>(l, xr, nullptr);
+        }
         return true;
     }
 
@@ -788,15 +794,17 @@ struct Consumer {
     // One warp per row: 16-byte chunks strided over the lanes, one shuffle
     // reduction per row.  K = 1024 inputs come from registers (xr), K = 2048 /
     // 3072 from the planar X vector.  The tiling matches for_tiles exactly.
-    template <int KIND>
-    __device__ __forceinline__ void mv_phase(int phase, int l, const float* xr, LmBest* bst) {
-        int a, b, T;
-        if (phase == PH_QKV) { a = S.qkv_a; b = S.qkv_b; T = QKV_TILE; }
-        else if (phase == PH_GU) { a = S.gu_a; b = S.gu_b; T = GU_TILE; }
-        else if (phase == PH_O) { a = S.o_a; b = S.o_b; T = O_TILE; }
-        else if (phase == PH_DOWN) { a = S.dn_a; b = S.dn_b; T = DOWN_TILE; }
-        else { a = S.lm_a; b = S.lm_b; T = LM_TILE; }
-        const int K = (phase == PH_O) ? QS : (phase == PH_DOWN ? I : H);
+    template <int KIND, int phase>
+    __device__ __forceinline__ void mv_phase(int l, const float* xr, LmBest* bst) {
+        int a, b;
+        constexpr int T = phase == PH_QKV ? QKV_TILE : phase == PH_GU ? GU_TILE : phase == PH_O ? O_TILE
+                          : phase == PH_DOWN ? DOWN_TILE : LM_TILE;
+        if (phase == PH_QKV) { a = S.qkv_a; b = S.qkv_b; }
+        else if (phase == PH_GU) { a = S.gu_a; b = S.gu_b; }
+        else if (phase == PH_O) { a = S.o_a; b = S.o_b; }
+        else if (phase == PH_DOWN) { a = S.dn_a; b = S.dn_b; }
+        else { a = S.lm_a; b = S.lm_b; }
+        constexpr int K = (phase == PH_O) ? QS : (phase == PH_DOWN ? I : H);
         const int R = b - a;
         const int ntiles = (R + T - 1) / T;
         const uint32_t tag = tag_of(S, l);
@@ -831,8 +839,8 @@ struct Consumer {
                             }
                         } else {
                             const uint4* w = reinterpret_cast<const uint4*>(st + lr * K * 2);
-                            const int CPL = K / 256;
-#pragma unroll 4
+                            constexpr int CPL = K / 256;
+#pragma unroll
                             for (int u = 0; u < CPL; ++u) {
                                 const int c = lane + 32 * u;
                                 acc[q] += dot8(w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
