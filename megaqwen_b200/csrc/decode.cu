@@ -939,8 +939,9 @@ struct Consumer {
     __device__ __forceinline__ void end_attn(AttnState& a, int l) {
         float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);   // [16][2][128]
         float* ml = reinterpret_cast<float*>(g_smem + SM_ML);     // [16][2][2]
-        if (ok && S.last && warp == 0) {
-            // the current position, from the bf16-rounded values in shared memory
+        if (ok && S.last && warp == NCW - 1) {
+            // the current position (on the warp with the fewest cached positions),
+            // from the bf16-rounded values in shared memory
             const float* kp = reinterpret_cast<const float*>(g_smem + SM_KP);
             const float* vp = reinterpret_cast<const float*>(g_smem + SM_VP);
             float k0 = kp[4 * lane], k1 = kp[4 * lane + 1], k2 = kp[4 * lane + 2], k3 = kp[4 * lane + 3];
@@ -971,7 +972,9 @@ struct Consumer {
         float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
         const int h = warp;  // warps 0 and 1 combine heads 0 and 1
         if (warp < 2) {
+#pragma unroll
             for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[w * 4 + 2 * h]);
+#pragma unroll
             for (int w = 0; w < NCW; ++w) {
                 float e = expf(ml[w * 4 + 2 * h] - M);
                 Ls += ml[w * 4 + 2 * h + 1] * e;
