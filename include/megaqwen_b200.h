@@ -171,6 +171,17 @@ int mq_decode_fetch(const void* workspace, int* token, uint32_t* error, uint32_t
 /* Number of CTAs the decode kernel would use on the current device. */
 int mq_decode_default_ctas(void);
 
+/* ---- prefill building block --------------------------------------------------
+ * mq_gemm_bf16: C[M, N] = A[M, K] . B[N, K]^T on the sm_100a tensor cores
+ * (tcgen05, fp32 accumulation in TMEM), A and B bf16 row-major (K contiguous,
+ * leading dimensions lda/ldb in elements).  Replaces the cublasGemmEx calls of
+ * the reference prefill (csrc/megakernel/fused_prefill.cu:674-824).
+ * epilogue: 0 store fp32, 1 add into fp32 C (residual), 2 C_bf16 =
+ * silu(A.B^T) * (A.B2^T) (gate/up), 3 store bf16.  N % 128 == 0, K % 64 == 0.
+ * err_flag: device int set non-zero if a bounded device wait ran out. */
+int mq_gemm_bf16(const void* A, int lda, const void* B, int ldb, const void* B2, void* C, int ldc, int M, int N,
+                 int K, int epilogue, int* err_flag, cudaStream_t stream);
+
 /* Last status recorded by the reference-ABI launchers on this host thread. */
 int mq_get_last_error(void);
 const char* mq_error_string(int code);

@@ -29,8 +29,8 @@ LIB = LIBDIR / "libmegaqwen_b200.so"
 EXT = PKG / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CUDA_SOURCES = ["decode.cu"]
-CUDA_HEADERS = ["mq_ptx.cuh"]
+CUDA_SOURCES = ["decode.cu", "prefill.cu"]
+CUDA_HEADERS = ["mq_ptx.cuh", "mq_tc.cuh", "gemm_tc.cuh"]
 
 
 def _nvcc() -> str:
