@@ -39,6 +39,22 @@ def bytes_per_token(pos: int) -> int:
     return WEIGHT_BYTES + KV_BYTES_PER_POS * (pos + 2)
 
 
+def prefill_flops(B, S):
+    """Dense FLOPs of a B x S prefill: linear layers 2 x 440,401,920 per token,
+    causal attention 28 * 16 * 4 * 128 * S(S+1)/2 per sequence, LM head of the
+    last token per sequence."""
+    return B * (S * 2 * 440_401_920 + 28 * 16 * 4 * 128 * S * (S + 1) / 2 + 2 * 151936 * 1024)
+
+
+def measured_bf16_tflops():
+    here = os.path.dirname(os.path.abspath(__file__))
+    try:
+        with open(os.path.join(here, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
 def measured_hbm_gbs():
     here = os.path.dirname(os.path.abspath(__file__))
     try:
@@ -276,18 +292,35 @@ def run_ours(args, rank, world, local):
             pm = P + 3 + n // 2
             sweep[str(P)] = {"tok_s": round(n / (tot / 1000.0), 1),
                              "roofline_frac": round(bytes_per_token(pm) / (lm / 1000.0) / 1e9 / hbm, 4)}
-        # prefill of 2048 tokens (config 4 shape, batch 1) through prefill_step
-        pre = megaqwen_b200.MegakernelPrefillDecoder(w.embed, w.layer_weights_flat(), w.final_norm, w.lm_head, cos,
-                                                     sin, 28, max_pos + 8, 2048)
-        ids = seeded_prompt(2048, seed=4)
-        pre.prefill_step(ids[:64])
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        pre.prefill_step(ids)
-        torch.cuda.synchronize()
-        pf = 2048 / (time.perf_counter() - t0)
-        sweep_prefill = {"S": 2048, "batch": 1, "tok_s": round(pf, 1)}
-        del pre
+        # prefill (config 4): batch 1 and 8, 2048-token prompts, tensor-core path
+        sweep_prefill = {}
+        peak_tf, peak_kind = measured_bf16_tflops()
+        for B in (1, 8):
+            S = 2048
+            ids = torch.stack([seeded_prompt(S, seed=4 + b) for b in range(B)]).to(dev)
+            kc = torch.zeros(B, 28, 8, S + 8, 128, dtype=torch.bfloat16, device=dev)
+            vc = torch.zeros_like(kc)
+            wsb = torch.empty(megaqwen_b200._C.prefill_workspace_bytes(B, S), dtype=torch.uint8, device=dev)
+            run = lambda: megaqwen_b200._C.prefill_batch(w.embed, w.layer_weights_flat(), w.final_norm, w.lm_head,
+                                                         cos, sin, ids, kc, vc, None, wsb)  # noqa: E731
+            for _ in range(2):
+                run()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = 3
+            e0.record()
+            for _ in range(reps):
+                run()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / reps
+            flops = prefill_flops(B, S)
+            sweep_prefill[f"B{B}_S{S}"] = {"tok_s": round(B * S / (ms / 1000.0), 1), "ms": round(ms, 3),
+                                           "tflops": round(flops / (ms / 1000.0) / 1e12, 1),
+                                           "frac_of_bf16_peak": round(flops / (ms / 1000.0) / 1e12 / peak_tf, 4),
+                                           "peak_tflops": peak_tf, "peak_kind": peak_kind}
+            del kc, vc, wsb
+            torch.cuda.empty_cache()
     else:
         sweep_prefill = None
 

@@ -182,6 +182,55 @@ int mq_decode_default_ctas(void);
 int mq_gemm_bf16(const void* A, int lda, const void* B, int ldb, const void* B2, void* C, int ldc, int M, int N,
                  int K, int epilogue, int* err_flag, cudaStream_t stream);
 
+/* ---- prefill ------------------------------------------------------------------
+ * mq_prefill: prompts of `batch` sequences x `seq_len` tokens, positions
+ * 0..seq_len-1, through all layers on the tensor cores (tcgen05 GEMMs, flash
+ * attention), writing each sequence's K/V cache rows and its greedy next token.
+ * Replaces launch_prefill_float (csrc/megakernel/fused_prefill.cu:601-867) and
+ * extends it to batches.  Sequence b's caches start at k_cache/v_cache +
+ * b * cache_seq_stride elements, each [num_layers, 8, max_seq_len, 128]. */
+typedef struct mq_prefill_params {
+    const int* ids;                        /* device int32 [batch * seq_len] */
+    int batch;
+    int seq_len;
+    int start_pos;                         /* must be 0 */
+    const void* embed;
+    const LDGLayerWeights* layers_host;    /* HOST array [num_layers] (as the reference passes) */
+    const void* final_norm;
+    const void* lm_head;
+    const void* cos_table;
+    const void* sin_table;
+    void* k_cache;
+    void* v_cache;
+    long long cache_seq_stride;            /* elements between sequences' caches */
+    int num_layers;
+    int max_seq_len;
+    float attn_scale;
+    int* out_tokens;                       /* device int32 [batch] */
+    float* logits;                         /* device fp32 [batch, 151936], optional */
+    void* hidden_out;                      /* unused, reserved */
+    void* workspace;                       /* device, mq_prefill_workspace_bytes(batch, seq_len) */
+    size_t workspace_bytes;
+    int* err_flag;                         /* optional device int: set when a device wait ran out */
+} mq_prefill_params;
+
+size_t mq_prefill_workspace_bytes(int batch, int seq_len);
+int mq_prefill(const mq_prefill_params* params, cudaStream_t stream);
+
+/* launch_prefill_float: the reference prefill launcher, same arguments
+ * (fused_prefill.cu:601-636).  layer_weights is a HOST array as in the
+ * reference; the bf16 scratch buffers and the cuBLAS handle are accepted and
+ * not used (the engine keeps a per-device workspace, allocated on first use). */
+void launch_prefill_float(const int* input_token_ids, int* output_token_id, int seq_len, const void* embed_weight,
+                          const PrefillLayerWeights* layer_weights, const void* final_norm_weight,
+                          const void* lm_head_weight, const void* cos_table, const void* sin_table, void* k_cache,
+                          void* v_cache, void* hidden_bf16, void* residual, void* normalized, void* q_proj,
+                          void* k_proj, void* v_proj, void* attn_out, void* o_proj_out, void* mlp_norm,
+                          void* gate_out, void* up_out, void* mlp_intermediate, void* down_out, void* final_hidden,
+                          void* block_max_vals, void* block_max_idxs, void* hidden_bf16_out, int num_layers,
+                          int max_seq_len, float attn_scale, void* cublas_handle, cudaStream_t stream);
+int mq_prefill_get_last_error(void);
+
 /* Last status recorded by the reference-ABI launchers on this host thread. */
 int mq_get_last_error(void);
 const char* mq_error_string(int code);

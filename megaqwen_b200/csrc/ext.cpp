@@ -121,6 +121,7 @@ public:
         std::vector<LDGLayerWeights> host(num_layers);
         for (int i = 0; i < num_layers; ++i) host[i] = make_layer(layer_weights_flat, (size_t)i * 11);
         d_layers_ = layer_table(host, device_);
+        layers_host_ = host;
         auto bf = torch::dtype(torch::kBFloat16).device(device_);
         auto f32 = torch::dtype(torch::kFloat32).device(device_);
         auto i32 = torch::dtype(torch::kInt32).device(device_);
@@ -287,13 +288,14 @@ protected:
     torch::Device device_{torch::kCUDA, 0};
     torch::Tensor embed_, final_norm_, lm_head_, cos_, sin_, d_layers_;
     std::vector<torch::Tensor> layer_tensors_;
+    std::vector<LDGLayerWeights> layers_host_;
     torch::Tensor k_cache_, v_cache_, hidden_buffer_, g_normalized_, output_token_, dev_position_, workspace_;
 };
 
-// Prefill + decode.  prefill_step runs the prompt through the decode engine one
-// position at a time with device-side token feed, synchronising once at the
-// end (the reference's cuBLAS prefill, fused_prefill.cu:601-867, computes the
-// same function).
+// Prefill + decode.  prefill_step runs the prompt through the tensor-core
+// prefill (mq_prefill: tcgen05 GEMMs, flash attention) and writes the K/V
+// cache rows 0..S-1, like the reference's cuBLAS prefill (fused_prefill.cu:
+// 601-867); decode_step then continues at position S.
 class MegakernelPrefillDecoder : public MegakernelDecoder {
 public:
     MegakernelPrefillDecoder(torch::Tensor embed_weight, std::vector<torch::Tensor> layer_weights_flat,
@@ -304,21 +306,72 @@ public:
           max_prefill_len_(max_prefill_len) {
         c10::cuda::CUDAGuard guard(device_);
         input_tokens_ = torch::zeros({std::max(1, max_prefill_len)}, torch::dtype(torch::kInt32).device(device_));
+        err_ = torch::zeros({1}, torch::dtype(torch::kInt32).device(device_));
     }
 
     int prefill_step(torch::Tensor input_token_ids) {
-        // megakernel_decode.py:496-549: checks, H2D copy, positions 0..S-1.
-        int seq_len = (int)input_token_ids.size(0);
-        if (seq_len > max_prefill_len_) throw std::runtime_error("Prefill sequence length exceeds maximum");
-        if (seq_len == 0) throw std::runtime_error("Empty input sequence");
-        if (seq_len > max_seq_len_) throw std::runtime_error("Prefill sequence length exceeds max_seq_len");
+        const int seq_len = check_prompt(input_token_ids);
         c10::cuda::CUDAGuard guard(device_);
         input_tokens_.narrow(0, 0, seq_len).copy_(input_token_ids.to(torch::kInt32).to(device_));
         cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
-        auto cpu_ids = input_token_ids.to(torch::kCPU).to(torch::kInt64);
-        auto acc = cpu_ids.accessor<int64_t, 1>();
-        for (int i = 0; i < seq_len; ++i)
-            if (acc[i] < 0 || acc[i] >= kVocab) throw std::runtime_error("input token out of range");
+        const size_t need = mq_prefill_workspace_bytes(1, seq_len);
+        if (!pf_ws_.defined() || (size_t)pf_ws_.numel() < need)
+            pf_ws_ = torch::empty({(int64_t)need}, torch::dtype(torch::kUInt8).device(device_));
+        mq_prefill_params p = {};
+        p.ids = input_tokens_.data_ptr<int>();
+        p.batch = 1;
+        p.seq_len = seq_len;
+        p.embed = embed_.data_ptr();
+        p.layers_host = layers_host_.data();
+        p.final_norm = final_norm_.data_ptr();
+        p.lm_head = lm_head_.data_ptr();
+        p.cos_table = cos_.data_ptr();
+        p.sin_table = sin_.data_ptr();
+        p.k_cache = k_cache_.data_ptr();
+        p.v_cache = v_cache_.data_ptr();
+        p.cache_seq_stride = 0;
+        p.num_layers = num_layers_;
+        p.max_seq_len = max_seq_len_;
+        p.attn_scale = attn_scale_;
+        p.out_tokens = output_token_.data_ptr<int>();
+        p.logits = last_logits_requested_ ? ensure_logits() : nullptr;
+        p.workspace = pf_ws_.data_ptr();
+        p.workspace_bytes = (size_t)pf_ws_.numel();
+        p.err_flag = err_.data_ptr<int>();
+        int rc = mq_prefill(&p, stream);
+        if (rc) raise_engine(rc, 0, "prefill_step");
+        const int tok = output_token_.item<int>();
+        if (err_.item<int>() != 0) {
+            err_.zero_();
+            raise_engine(MQ_ERR_PIPE_TIMEOUT, 0, "prefill_step");
+        }
+        position_ = seq_len;
+        last_token_ = tok;
+        return tok;
+    }
+
+    // prefill_step that also returns the fp32 logits of the last position.
+    std::tuple<int, torch::Tensor> prefill_step_with_logits(torch::Tensor input_token_ids) {
+        last_logits_requested_ = true;
+        int tok;
+        try {
+            tok = prefill_step(input_token_ids);
+        } catch (...) {
+            last_logits_requested_ = false;
+            throw;
+        }
+        last_logits_requested_ = false;
+        return std::make_tuple(tok, logits_.clone());
+    }
+
+    // The prompt through the decode kernel one position at a time (device-side
+    // token feed, one host synchronisation): the reference decode-only
+    // generators' way of consuming a prompt (megakernel_decode.py:1166-1167).
+    int prefill_step_sequential(torch::Tensor input_token_ids) {
+        const int seq_len = check_prompt(input_token_ids);
+        c10::cuda::CUDAGuard guard(device_);
+        input_tokens_.narrow(0, 0, seq_len).copy_(input_token_ids.to(torch::kInt32).to(device_));
+        cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
         for (int i = 0; i < seq_len; ++i) {
             mq_decode_params p = params(0, nullptr);
             p.input_token_ptr = input_tokens_.data_ptr<int>() + i;
@@ -334,9 +387,81 @@ public:
     int max_prefill_len() const { return max_prefill_len_; }
 
 protected:
+    // megakernel_decode.py:496-504 checks, plus token range and max_seq_len.
+    int check_prompt(const torch::Tensor& ids) {
+        if (ids.dim() != 1) throw std::runtime_error("input_token_ids must be 1-D");
+        const int seq_len = (int)ids.size(0);
+        if (seq_len > max_prefill_len_) throw std::runtime_error("Prefill sequence length exceeds maximum");
+        if (seq_len == 0) throw std::runtime_error("Empty input sequence");
+        if (seq_len > max_seq_len_) throw std::runtime_error("Prefill sequence length exceeds max_seq_len");
+        auto cpu_ids = ids.to(torch::kCPU).to(torch::kInt64);
+        auto acc = cpu_ids.accessor<int64_t, 1>();
+        for (int i = 0; i < seq_len; ++i)
+            if (acc[i] < 0 || acc[i] >= kVocab) throw std::runtime_error("input token out of range");
+        return seq_len;
+    }
+    float* ensure_logits() {
+        if (!logits_.defined()) logits_ = torch::empty({kVocab}, torch::dtype(torch::kFloat32).device(device_));
+        return logits_.data_ptr<float>();
+    }
+
     int max_prefill_len_;
-    torch::Tensor input_tokens_;
+    bool last_logits_requested_ = false;
+    torch::Tensor input_tokens_, pf_ws_, err_, logits_;
 };
+
+// Batched prefill: ids int32 [B, S] on the GPU, caches
+// [B, L, 8, max_seq_len, 128] bf16; returns the greedy next token of each
+// sequence (device int32 [B]) and optionally writes logits [B, 151936].
+torch::Tensor prefill_batch(torch::Tensor embed, std::vector<torch::Tensor> layer_weights_flat, torch::Tensor final_norm,
+                            torch::Tensor lm_head, torch::Tensor cos, torch::Tensor sin, torch::Tensor ids,
+                            torch::Tensor k_cache, torch::Tensor v_cache, c10::optional<torch::Tensor> logits,
+                            c10::optional<torch::Tensor> workspace) {
+    if (ids.dim() != 2 || ids.scalar_type() != torch::kInt32 || !ids.is_cuda() || !ids.is_contiguous())
+        throw std::runtime_error("ids must be a contiguous int32 [B, S] CUDA tensor");
+    const int B = (int)ids.size(0), S = (int)ids.size(1);
+    const int L = (int)layer_weights_flat.size() / 11;
+    if (L < 1 || (int)layer_weights_flat.size() != L * 11) throw std::runtime_error("layer_weights_flat must hold L * 11 tensors");
+    if (k_cache.dim() != 5 || k_cache.size(0) != B || k_cache.size(1) != L || k_cache.size(2) != MQ_NUM_KV_HEADS ||
+        k_cache.size(4) != MQ_HEAD_DIM || k_cache.scalar_type() != torch::kBFloat16 || !k_cache.is_contiguous() ||
+        v_cache.sizes() != k_cache.sizes() || !v_cache.is_contiguous())
+        throw std::runtime_error("caches must be contiguous bf16 [B, L, 8, max_seq_len, 128]");
+    const int max_seq = (int)k_cache.size(3);
+    if (S > max_seq || S < 1) throw std::runtime_error("sequence length exceeds max_seq_len");
+    c10::cuda::CUDAGuard guard(ids.device());
+    std::vector<LDGLayerWeights> host(L);
+    for (int i = 0; i < L; ++i) host[i] = make_layer(layer_weights_flat, (size_t)i * 11);
+    const size_t need = mq_prefill_workspace_bytes(B, S);
+    torch::Tensor ws = (workspace.has_value() && (size_t)workspace->numel() >= need)
+                           ? *workspace
+                           : torch::empty({(int64_t)need}, torch::dtype(torch::kUInt8).device(ids.device()));
+    auto out = torch::empty({B}, torch::dtype(torch::kInt32).device(ids.device()));
+    auto err = torch::zeros({1}, torch::dtype(torch::kInt32).device(ids.device()));
+    mq_prefill_params p = {};
+    p.ids = ids.data_ptr<int>();
+    p.batch = B;
+    p.seq_len = S;
+    p.embed = embed.data_ptr();
+    p.layers_host = host.data();
+    p.final_norm = final_norm.data_ptr();
+    p.lm_head = lm_head.data_ptr();
+    p.cos_table = cos.data_ptr();
+    p.sin_table = sin.data_ptr();
+    p.k_cache = k_cache.data_ptr();
+    p.v_cache = v_cache.data_ptr();
+    p.cache_seq_stride = (long long)L * MQ_NUM_KV_HEADS * max_seq * MQ_HEAD_DIM;
+    p.num_layers = L;
+    p.max_seq_len = max_seq;
+    p.attn_scale = 1.0f / sqrtf(128.0f);
+    p.out_tokens = out.data_ptr<int>();
+    p.logits = logits.has_value() ? logits->data_ptr<float>() : nullptr;
+    p.workspace = ws.data_ptr();
+    p.workspace_bytes = (size_t)ws.numel();
+    p.err_flag = err.data_ptr<int>();
+    int rc = mq_prefill(&p, c10::cuda::getCurrentCUDAStream(ids.device().index()).stream());
+    if (rc) raise_engine(rc, 0, "prefill_batch");
+    return out;
+}
 
 // The reference's GEMV-megakernel prefill class for short prompts
 // (megakernel_decode.py:788-1053): same interface, max_prefill_len 64 by default.
@@ -489,6 +614,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
              py::arg("max_seq_len"), py::arg("max_prefill_len") = 512)
         .def("prefill_step", &MegakernelPrefillDecoder::prefill_step)
+        .def("prefill_step_with_logits", &MegakernelPrefillDecoder::prefill_step_with_logits)
+        .def("prefill_step_sequential", &MegakernelPrefillDecoder::prefill_step_sequential)
         .def("max_prefill_len", &MegakernelPrefillDecoder::max_prefill_len);
     py::class_<MegakernelFusedPrefillDecoder, MegakernelPrefillDecoder>(m, "MegakernelFusedPrefillDecoder")
         .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
@@ -502,5 +629,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("decode_ldg_with_logits", &decode_ldg_with_logits);
     m.def("workspace_bytes", []() { return (int64_t)mq_decode_workspace_bytes(); });
     m.def("default_ctas", []() { return mq_decode_default_ctas(); });
+    m.def("prefill_batch", &prefill_batch, py::arg("embed"), py::arg("layer_weights_flat"), py::arg("final_norm"),
+          py::arg("lm_head"), py::arg("cos"), py::arg("sin"), py::arg("ids"), py::arg("k_cache"), py::arg("v_cache"),
+          py::arg("logits") = py::none(), py::arg("workspace") = py::none());
+    m.def("prefill_workspace_bytes", [](int b, int s) { return (int64_t)mq_prefill_workspace_bytes(b, s); });
     m.def("version", []() { return std::string(mq_version()); });
 }

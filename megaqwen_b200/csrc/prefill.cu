@@ -97,3 +97,196 @@ extern "C" int mq_gemm_bf16(const void* A, int lda, const void* B, int ldb, cons
                             int N, int K, int epilogue, int* err_flag, cudaStream_t stream) {
     return mq::gemm_bf16(A, lda, B, ldb, B2, C, ldc, M, N, K, epilogue, err_flag, stream);
 }
+
+// =============================================================================
+// Prefill forward (batched): the reference's launch_prefill_float
+// (csrc/megakernel/fused_prefill.cu:601-867) on tcgen05 GEMMs.
+// =============================================================================
+#include "prefill_kernels.cuh"
+#include "attn_fa.cuh"
+
+namespace mq {
+namespace {
+
+struct PrefillLayout {
+    size_t X, Xn, QKV, Qb, Kb, Vb, Ob, act, lastn, logits, err, total;
+};
+
+PrefillLayout prefill_layout(int B, int S) {
+    const size_t M = (size_t)B * S;
+    PrefillLayout L;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o += (bytes + 255) & ~size_t(255); return r; };
+    L.X = take(M * 1024 * 4);
+    L.Xn = take(M * 1024 * 2);
+    L.QKV = take(M * 4096 * 4);
+    L.Qb = take(M * 2048 * 2);
+    L.Kb = take(M * 1024 * 2);
+    L.Vb = take(M * 1024 * 2);
+    L.Ob = take(M * 2048 * 2);
+    L.act = take(M * 3072 * 2);
+    L.lastn = take((size_t)B * 1024 * 2);
+    L.logits = take((size_t)B * MQ_VOCAB_SIZE * 4);
+    L.err = take(256);
+    L.total = o;
+    return L;
+}
+
+#define MQ_TRY(x)                       \
+    do {                                \
+        int rc_ = (x);                  \
+        if (rc_ != MQ_OK) return rc_;   \
+    } while (0)
+
+}  // namespace
+
+int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
+    if (!p || !p->ids || !p->embed || !p->layers_host || !p->final_norm || !p->lm_head || !p->cos_table ||
+        !p->sin_table || !p->k_cache || !p->v_cache || !p->out_tokens || !p->workspace)
+        return MQ_ERR_INVALID_ARGUMENT;
+    const int B = p->batch, S = p->seq_len;
+    if (B < 1 || S < 1 || p->num_layers < 1 || p->num_layers > MQ_MAX_LAYERS) return MQ_ERR_INVALID_ARGUMENT;
+    if (p->start_pos != 0 || S > p->max_seq_len) return MQ_ERR_INVALID_ARGUMENT;
+    const PrefillLayout L = prefill_layout(B, S);
+    if (p->workspace_bytes < L.total) return MQ_ERR_WORKSPACE;
+    uint8_t* ws = (uint8_t*)p->workspace;
+    float* X = (float*)(ws + L.X);
+    pf::bf16* Xn = (pf::bf16*)(ws + L.Xn);
+    float* QKV = (float*)(ws + L.QKV);
+    pf::bf16* Qb = (pf::bf16*)(ws + L.Qb);
+    pf::bf16* Kb = (pf::bf16*)(ws + L.Kb);
+    pf::bf16* Vb = (pf::bf16*)(ws + L.Vb);
+    pf::bf16* Ob = (pf::bf16*)(ws + L.Ob);
+    pf::bf16* act = (pf::bf16*)(ws + L.act);
+    pf::bf16* lastn = (pf::bf16*)(ws + L.lastn);
+    float* logits = p->logits ? p->logits : (float*)(ws + L.logits);
+    int* err = p->err_flag ? p->err_flag : (int*)(ws + L.err);
+    const int M = B * S;
+    const float scale_log2 = p->attn_scale * 1.4426950408889634f;
+
+    {
+        static bool fa_configured[64] = {false};
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return MQ_ERR_CUDA;
+        if (!fa_configured[dev]) {
+            if (cudaFuncSetAttribute(pf::flash_attn_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     pf::FA_SMEM) != cudaSuccess)
+                return MQ_ERR_CUDA;
+            fa_configured[dev] = true;
+        }
+    }
+    pf::embed_kernel<<<(M + 7) / 8, 256, 0, st>>>(p->ids, (const pf::bf16*)p->embed, X, M);
+    for (int l = 0; l < p->num_layers; ++l) {
+        const LDGLayerWeights& W = p->layers_host[l];
+        pf::rmsnorm_bf16_kernel<<<(M + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)W.input_layernorm_weight, Xn, M, 1, 0);
+        MQ_TRY(gemm_bf16(Xn, 1024, W.q_proj_weight, 1024, nullptr, QKV, 4096, M, 2048, 1024, EPI_STORE_F32, err, st));
+        MQ_TRY(gemm_bf16(Xn, 1024, W.k_proj_weight, 1024, nullptr, QKV + 2048, 4096, M, 1024, 1024, EPI_STORE_F32, err,
+                         st));
+        MQ_TRY(gemm_bf16(Xn, 1024, W.v_proj_weight, 1024, nullptr, QKV + 3072, 4096, M, 1024, 1024, EPI_STORE_F32, err,
+                         st));
+        pf::QkvArgs qa;
+        qa.qkv = QKV;
+        qa.q_norm = (const pf::bf16*)W.q_norm_weight;
+        qa.k_norm = (const pf::bf16*)W.k_norm_weight;
+        qa.cos_table = (const pf::bf16*)p->cos_table;
+        qa.sin_table = (const pf::bf16*)p->sin_table;
+        qa.Qb = Qb;
+        qa.Kb = Kb;
+        qa.Vb = Vb;
+        const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * MQ_HEAD_DIM;
+        qa.k_cache = (pf::bf16*)p->k_cache + layer_off;
+        qa.v_cache = (pf::bf16*)p->v_cache + layer_off;
+        qa.cache_seq_stride = p->cache_seq_stride;
+        qa.S = S;
+        qa.start_pos = 0;
+        qa.max_seq_len = p->max_seq_len;
+        pf::qknorm_rope_kernel<<<M, 1024, 0, st>>>(qa);
+        dim3 fgrid((S + pf::FA_B - 1) / pf::FA_B, MQ_NUM_Q_HEADS, B);
+        pf::flash_attn_causal_kernel<<<fgrid, 128, pf::FA_SMEM, st>>>(Qb, Kb, Vb, Ob, S, scale_log2);
+        MQ_TRY(gemm_bf16(Ob, 2048, W.o_proj_weight, 2048, nullptr, X, 1024, M, 1024, 2048, EPI_ADD_F32, err, st));
+        pf::rmsnorm_bf16_kernel<<<(M + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)W.post_attn_layernorm_weight, Xn, M,
+                                                               1, 0);
+        MQ_TRY(gemm_bf16(Xn, 1024, W.gate_proj_weight, 1024, W.up_proj_weight, act, 3072, M, 3072, 1024, EPI_SILU_MUL,
+                         err, st));
+        MQ_TRY(gemm_bf16(act, 3072, W.down_proj_weight, 3072, nullptr, X, 1024, M, 1024, 3072, EPI_ADD_F32, err, st));
+    }
+    // last position of each sequence: final norm, tied LM head, argmax
+    pf::rmsnorm_bf16_kernel<<<(B + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)p->final_norm, lastn, B, S, S - 1);
+    MQ_TRY(gemm_bf16(lastn, 1024, p->lm_head, 1024, nullptr, logits, MQ_VOCAB_SIZE, B, MQ_VOCAB_SIZE, 1024,
+                     EPI_STORE_F32, err, st));
+    pf::argmax_kernel<<<B, 1024, 0, st>>>(logits, MQ_VOCAB_SIZE, MQ_VOCAB_SIZE, p->out_tokens);
+    return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+}
+
+size_t prefill_workspace_bytes(int batch, int seq_len) { return prefill_layout(batch, seq_len).total; }
+
+}  // namespace mq
+
+namespace {
+std::mutex g_pf_mutex;
+struct PfWs {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+PfWs g_pf_ws[64];
+thread_local int g_pf_last_error = 0;
+}  // namespace
+
+extern "C" {
+
+size_t mq_prefill_workspace_bytes(int batch, int seq_len) { return mq::prefill_workspace_bytes(batch, seq_len); }
+
+int mq_prefill(const mq_prefill_params* params, cudaStream_t stream) { return mq::prefill_forward(params, stream); }
+
+void launch_prefill_float(const int* input_token_ids, int* output_token_id, int seq_len, const void* embed_weight,
+                          const PrefillLayerWeights* layer_weights, const void* final_norm_weight,
+                          const void* lm_head_weight, const void* cos_table, const void* sin_table, void* k_cache,
+                          void* v_cache, void* /*hidden_bf16*/, void* /*residual*/, void* /*normalized*/,
+                          void* /*q_proj*/, void* /*k_proj*/, void* /*v_proj*/, void* /*attn_out*/,
+                          void* /*o_proj_out*/, void* /*mlp_norm*/, void* /*gate_out*/, void* /*up_out*/,
+                          void* /*mlp_intermediate*/, void* /*down_out*/, void* /*final_hidden*/,
+                          void* /*block_max_vals*/, void* /*block_max_idxs*/, void* /*hidden_bf16_out*/,
+                          int num_layers, int max_seq_len, float attn_scale, void* /*cublas_handle*/,
+                          cudaStream_t stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) { g_pf_last_error = MQ_ERR_CUDA; return; }
+    const size_t need = mq::prefill_workspace_bytes(1, seq_len);
+    void* ws = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_pf_mutex);
+        if (g_pf_ws[dev].bytes < need) {
+            if (g_pf_ws[dev].ptr) {
+                cudaStreamSynchronize(stream);
+                cudaFree(g_pf_ws[dev].ptr);
+            }
+            g_pf_ws[dev].ptr = nullptr;
+            g_pf_ws[dev].bytes = 0;
+            if (cudaMalloc(&g_pf_ws[dev].ptr, need) != cudaSuccess) { g_pf_last_error = MQ_ERR_CUDA; return; }
+            g_pf_ws[dev].bytes = need;
+        }
+        ws = g_pf_ws[dev].ptr;
+    }
+    mq_prefill_params p = {};
+    p.ids = input_token_ids;
+    p.batch = 1;
+    p.seq_len = seq_len;
+    p.embed = embed_weight;
+    p.layers_host = layer_weights;
+    p.final_norm = final_norm_weight;
+    p.lm_head = lm_head_weight;
+    p.cos_table = cos_table;
+    p.sin_table = sin_table;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.num_layers = num_layers;
+    p.max_seq_len = max_seq_len;
+    p.attn_scale = attn_scale;
+    p.out_tokens = output_token_id;
+    p.workspace = ws;
+    p.workspace_bytes = need;
+    g_pf_last_error = mq::prefill_forward(&p, stream);
+}
+
+int mq_prefill_get_last_error(void) { return g_pf_last_error; }
+
+}  // extern "C"
