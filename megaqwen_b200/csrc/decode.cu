@@ -1249,14 +1249,20 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     int dev = 0;
     cudaError_t ce = cudaGetDevice(&dev);
     if (ce != cudaSuccess) return cuda_fail(ce, "cudaGetDevice");
-    int rc = configure_kernel(dev);
-    if (rc) return rc;
-    int G = p->num_ctas > 0 ? p->num_ctas : default_ctas(dev);
+    // Per-device set-up (kernel attribute, SM count, occupancy check), once.
+    static int dev_ctas[64] = {0};
+    if (dev < 0 || dev >= 64) return note(MQ_ERR_INVALID_ARGUMENT, "device index above 63");
+    if (!dev_ctas[dev]) {
+        int rc = configure_kernel(dev);
+        if (rc) return rc;
+        int maxb = 0;
+        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel, mq::NTHREADS, mq::SMEM_BYTES);
+        if (ce != cudaSuccess) return cuda_fail(ce, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (maxb < 1) return note(MQ_ERR_CUDA, "decode kernel does not fit on one SM (occupancy 0)");
+        dev_ctas[dev] = default_ctas(dev);
+    }
+    int G = p->num_ctas > 0 ? p->num_ctas : dev_ctas[dev];
     if (G < mq::NKV || G > mq::MAX_CTAS) return MQ_ERR_INVALID_ARGUMENT;
-    int maxb = 0;
-    ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel, mq::NTHREADS, mq::SMEM_BYTES);
-    if (ce != cudaSuccess) return cuda_fail(ce, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
-    if (maxb < 1) return note(MQ_ERR_CUDA, "decode kernel does not fit on one SM (occupancy 0)");
     mq::KParams k;
     k.input_token = p->input_token;
     k.input_token_ptr = p->input_token_ptr;
@@ -1283,17 +1289,20 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     k.inject_skip_cta = p->inject_skip_cta;
     k.trace = p->trace;
     {
-        // experiment hooks (handoff polling strategy)
-        const char* e = getenv("MQ_POLL_MODE");
-        k.poll_mode = e ? atoi(e) : 2;
-        e = getenv("MQ_POLL_WARPS");
-        k.poll_warps = e ? atoi(e) : mq::NCW;
-        e = getenv("MQ_POLL_SLEEP");
-        k.poll_sleep_ns = e ? atoi(e) : 0;
-        e = getenv("MQ_STORE_MODE");
-        k.store_mode = e ? atoi(e) : 0;
-        e = getenv("MQ_ARRIVE_RELAXED");
-        k.arrive_relaxed = e ? atoi(e) : 1;
+        // tuning knobs, read from the environment once per process
+        struct Knobs {
+            int poll_mode, poll_warps, poll_sleep, store_mode, arrive_relaxed;
+        };
+        static const Knobs kn = [] {
+            auto env = [](const char* n, int d) { const char* e = getenv(n); return e ? atoi(e) : d; };
+            return Knobs{env("MQ_POLL_MODE", 2), env("MQ_POLL_WARPS", mq::NCW), env("MQ_POLL_SLEEP", 0),
+                         env("MQ_STORE_MODE", 0), env("MQ_ARRIVE_RELAXED", 1)};
+        }();
+        k.poll_mode = kn.poll_mode;
+        k.poll_warps = kn.poll_warps;
+        k.poll_sleep_ns = kn.poll_sleep;
+        k.store_mode = kn.store_mode;
+        k.arrive_relaxed = kn.arrive_relaxed;
     }
 
     cudaLaunchConfig_t cfg = {};
