@@ -231,6 +231,44 @@ void launch_prefill_float(const int* input_token_ids, int* output_token_id, int 
                           int max_seq_len, float attn_scale, void* cublas_handle, cudaStream_t stream);
 int mq_prefill_get_last_error(void);
 
+/* ---- batched decode -----------------------------------------------------------
+ * mq_decode_batch: one greedy decode step for `batch` (1..128) independent
+ * sequences.  Sequence b consumes tokens[b] at position positions[b], appends
+ * its K/V rows there, and on return (stream order) tokens[b] holds its next
+ * token and positions[b] has advanced by one.  The weights are read once per
+ * step for all sequences (small-batch tcgen05 GEMMs, split-K).  This is the
+ * batch >= 16 serving path the reference drives through its per-sequence
+ * decoder (csrc/megakernel/ldg_decode.cu launch_ldg_decode called once per
+ * sequence); numerics follow the single-sequence decode with bf16 GEMM
+ * operands.  max_context >= max_b(positions[b] + 1) bounds the attention grid
+ * (host-known, so a step needs no device->host read).  Caches as in
+ * mq_prefill_params. */
+typedef struct mq_decode_batch_params {
+    int* tokens;                           /* device int32 [batch], in/out */
+    int* positions;                        /* device int32 [batch], in/out */
+    int batch;
+    int max_context;
+    const void* embed;
+    const LDGLayerWeights* layers_host;    /* HOST array [num_layers] */
+    const void* final_norm;
+    const void* lm_head;
+    const void* cos_table;
+    const void* sin_table;
+    void* k_cache;
+    void* v_cache;
+    long long cache_seq_stride;
+    int num_layers;
+    int max_seq_len;
+    float attn_scale;
+    float* logits;                         /* device fp32 [batch, 151936], optional */
+    void* workspace;                       /* device, mq_decode_batch_workspace_bytes(batch, max_seq_len) */
+    size_t workspace_bytes;
+    int* err_flag;                         /* device int: set when a device wait ran out (required) */
+} mq_decode_batch_params;
+
+size_t mq_decode_batch_workspace_bytes(int batch, int max_seq_len);
+int mq_decode_batch(const mq_decode_batch_params* params, cudaStream_t stream);
+
 /* Last status recorded by the reference-ABI launchers on this host thread. */
 int mq_get_last_error(void);
 const char* mq_error_string(int code);

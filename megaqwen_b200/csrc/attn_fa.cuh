@@ -51,7 +51,7 @@ __device__ __forceinline__ void fa_load_tile(__nv_bfloat16* dst, const __nv_bflo
     }
 }
 
-__global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __nv_bfloat16* __restrict__ Q,
+static __global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __nv_bfloat16* __restrict__ Q,
                                                                 const __nv_bfloat16* __restrict__ K,
                                                                 const __nv_bfloat16* __restrict__ V,
                                                                 __nv_bfloat16* __restrict__ O, int S,

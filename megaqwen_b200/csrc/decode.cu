@@ -1314,7 +1314,8 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    static const int coop = [] { const char* e = getenv("MQ_COOP"); return e ? atoi(e) : 1; }();
+    cfg.numAttrs = coop ? 1 : 0;
     cudaError_t e = cudaLaunchKernelEx(&cfg, mq::decode_step_kernel, k);
     if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(decode_step_kernel, cooperative)");
     return MQ_OK;
@@ -1493,3 +1494,9 @@ const char* mq_error_string(int code) {
 const char* mq_version(void) { return "megaqwen_b200 0.1"; }
 
 }  // extern "C"
+
+namespace mq {
+// Records the failing CUDA call for mq_last_error_detail (used by the other
+// translation units of the library); returns MQ_ERR_CUDA.
+int note_cuda(cudaError_t e, const char* what) { return cuda_fail(e, what); }
+}  // namespace mq

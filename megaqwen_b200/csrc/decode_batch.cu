@@ -1,0 +1,611 @@
+// Batched decode (B independent sequences, one token each per step) for
+// sm_100a: the weights are streamed once per step for all B tokens through
+// the small-batch tcgen05 GEMM (gemm_tc_small_kernel: weights on the MMA's
+// 128-row side, tokens on its N side, split-K with fp32 red.add); attention is
+// split-K over each sequence's own cache length; norms, RoPE, SiLU and argmax
+// are the prefill kernels.  No host synchronisation inside a step.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstdlib>
+#include <mutex>
+
+#include "gemm_small.cuh"
+#include "megaqwen_b200.h"
+#include "prefill_kernels.cuh"
+#include "attn_fa.cuh"
+
+namespace mq {
+
+bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows);
+int note_cuda(cudaError_t e, const char* what);
+
+namespace db {
+
+typedef __nv_bfloat16 bf16;
+constexpr int D = MQ_HEAD_DIM;
+constexpr int ATT_CHUNK = 256;       // cache positions per attention work unit (4 warps x 4 groups of 16)
+constexpr int PART = 132;            // floats per (unit, head): m, l, pad, pad, acc[128]
+
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
+// Output dimension held by accumulator row g of 8x8 block (u, r) after the
+// in-register transpose of a 16-byte-per-lane row load (lane t loads dims
+// 32u + 8t .. 32u + 8t + 7, register r holds the pair 32u + 8t + 2r).
+__device__ __forceinline__ int vdim(int u, int r, int g) { return 32 * u + 8 * (g >> 1) + 2 * r + (g & 1); }
+
+// One unit = (chunk c, kv head h, sequence b), 4 warps: both q heads of kv
+// head h against cache positions [c*256, min(L, c*256+256)), L = pos[b] + 1
+// (the row at pos[b] was written by this step's QK-norm/RoPE kernel).  Warp w
+// takes the 16-position groups w, w+4, .. of the chunk.
+//
+// No shared-memory staging: each lane loads 16-byte pieces of K and V rows
+// straight into registers.  S^T = K Q^T runs on mma.sync m16n8k16 with 16
+// positions as the M side and the q heads as N (heads 0/1 real, the others
+// zero); the summation order over head dims is permuted consistently in Q and
+// K so the 16-byte pieces are the A fragments as loaded.  O^T = V^T P^T takes
+// V^T and P^T from movmatrix transposes of the loaded V rows and of the
+// exponentiated scores.  Online softmax in the log2 domain (q pre-scaled by
+// scale * log2 e); the four warps merge through shared memory and the unit
+// writes its (max, sum, unnormalised acc) per q head.
+__global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict__ Qf, const bf16* __restrict__ kc,
+                                                        const bf16* __restrict__ vc, const int* __restrict__ pos,
+                                                        long long seq_stride, int max_seq, int C, float scale_log2,
+                                                        float* __restrict__ part) {
+    __shared__ float sm_ml[4][4];
+    __shared__ float sm_acc[4][2][D];
+    pdl_wait();
+    pdl_trigger();
+    const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int L = pos[b] + 1, p0 = c * ATT_CHUNK;
+    float* pp = part + (((size_t)b * 8 + h) * C + c) * 2 * PART;
+    if (p0 >= L) {
+        if (threadIdx.x < 2) {
+            pp[threadIdx.x * PART] = -INFINITY;
+            pp[threadIdx.x * PART + 1] = 0.f;
+        }
+        return;
+    }
+    const int n = min(ATT_CHUNK, L - p0);
+    const int ngroups = (n + 15) >> 4;
+    const bf16* kb = kc + b * seq_stride + ((size_t)h * max_seq + p0) * D;
+    const bf16* vb = vc + b * seq_stride + ((size_t)h * max_seq + p0) * D;
+
+    // B fragments of Q^T: lane (g, t), g < 2 = q head 2h+g; k-step (u, half)
+    uint32_t qb[4][2][2];
+    {
+        const float* q = Qf + (size_t)b * 2048 + (2 * h + (g & 1)) * D;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const int d0 = 32 * u + 8 * t + 4 * hf;
+                if (g < 2) {
+                    qb[u][hf][0] = pf::pack_bf16(q[d0] * scale_log2, q[d0 + 1] * scale_log2);
+                    qb[u][hf][1] = pf::pack_bf16(q[d0 + 2] * scale_log2, q[d0 + 3] * scale_log2);
+                } else {
+                    qb[u][hf][0] = qb[u][hf][1] = 0u;
+                }
+            }
+    }
+    float oacc[4][2][4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) oacc[u][qq][0] = oacc[u][qq][1] = oacc[u][qq][2] = oacc[u][qq][3] = 0.f;
+    float mrun[2] = {-INFINITY, -INFINITY}, lrun[2] = {0.f, 0.f};
+
+    uint4 kr[2][4], vr[2][4];
+    auto load = [&](int grp, uint4 (&k)[2][4], uint4 (&v)[2][4]) {
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+            const int row = 16 * grp + 8 * hr + g;
+            const bool ok = row < n;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const size_t off = (size_t)row * D + 32 * u + 8 * t;
+                k[hr][u] = ok ? *reinterpret_cast<const uint4*>(kb + off) : make_uint4(0, 0, 0, 0);
+                v[hr][u] = ok ? *reinterpret_cast<const uint4*>(vb + off) : make_uint4(0, 0, 0, 0);
+            }
+        }
+    };
+    if (warp < ngroups) load(warp, kr, vr);
+    for (int grp = warp; grp < ngroups; grp += 4) {
+        uint4 kn[2][4], vn[2][4];
+        const bool more = grp + 4 < ngroups;
+        if (more) load(grp + 4, kn, vn);
+        // S^T[16 positions][8 heads]
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t r0[4] = {kr[0][u].x, kr[0][u].y, kr[0][u].z, kr[0][u].w};
+            const uint32_t r1[4] = {kr[1][u].x, kr[1][u].y, kr[1][u].z, kr[1][u].w};
+#pragma unroll
+            for (int hf = 0; hf < 2; ++hf) {
+                const uint32_t a[4] = {r0[2 * hf], r1[2 * hf], r0[2 * hf + 1], r1[2 * hf + 1]};
+                pf::mma_bf16(s, a, qb[u][hf][0], qb[u][hf][1]);
+            }
+        }
+        // s[0], s[1]: position g, heads 2t, 2t+1; s[2], s[3]: position g + 8
+        const int pa = 16 * grp + g, pb = pa + 8;
+        if (pa >= n) s[0] = s[1] = -INFINITY;
+        if (pb >= n) s[2] = s[3] = -INFINITY;
+        float mx[2] = {fmaxf(s[0], s[2]), fmaxf(s[1], s[3])};
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
+            mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o));
+        }
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float mn = fmaxf(mrun[r], mx[r]);
+            corr[r] = exp2f(mrun[r] - mn);
+            mrun[r] = mn;
+            lrun[r] *= corr[r];
+        }
+        const float e0 = exp2f(s[0] - mrun[0]), e1 = exp2f(s[1] - mrun[1]);
+        const float e2 = exp2f(s[2] - mrun[0]), e3 = exp2f(s[3] - mrun[1]);
+        lrun[0] += e0 + e2;
+        lrun[1] += e1 + e3;
+        // P^T as the B operand (k = position, n = head): transposes of the score blocks
+        const uint32_t pb0 = movm_t(pf::pack_bf16(e0, e1));
+        const uint32_t pb1 = movm_t(pf::pack_bf16(e2, e3));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t r0[4] = {vr[0][u].x, vr[0][u].y, vr[0][u].z, vr[0][u].w};
+            const uint32_t r1[4] = {vr[1][u].x, vr[1][u].y, vr[1][u].z, vr[1][u].w};
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) {
+                float* o = oacc[u][qq];
+                o[0] *= corr[0]; o[1] *= corr[1]; o[2] *= corr[0]; o[3] *= corr[1];
+                const uint32_t a[4] = {movm_t(r0[qq]), movm_t(r0[qq + 2]), movm_t(r1[qq]), movm_t(r1[qq + 2])};
+                pf::mma_bf16(o, a, pb0, pb1);
+            }
+        }
+        if (more) {
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    kr[hr][u] = kn[hr][u];
+                    vr[hr][u] = vn[hr][u];
+                }
+        }
+    }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+        lrun[0] += __shfl_xor_sync(0xffffffffu, lrun[0], o);
+        lrun[1] += __shfl_xor_sync(0xffffffffu, lrun[1], o);
+    }
+    // lanes with t == 0 hold heads 0/1: c0/c1 at dim row g, c2/c3 at dim row g + 8
+    if (t == 0) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) {
+                const int d0 = vdim(u, qq, g), d1 = vdim(u, qq + 2, g);
+                sm_acc[warp][0][d0] = oacc[u][qq][0];
+                sm_acc[warp][1][d0] = oacc[u][qq][1];
+                sm_acc[warp][0][d1] = oacc[u][qq][2];
+                sm_acc[warp][1][d1] = oacc[u][qq][3];
+            }
+        if (lane == 0) {
+            sm_ml[warp][0] = mrun[0];
+            sm_ml[warp][1] = mrun[1];
+            sm_ml[warp][2] = lrun[0];
+            sm_ml[warp][3] = lrun[1];
+        }
+    }
+    __syncthreads();
+    const int d = threadIdx.x;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[w][r]);
+        float A = 0.f, Ls = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            if (sm_ml[w][r] == -INFINITY) continue;   // warp saw no positions
+            const float e = exp2f(sm_ml[w][r] - M);
+            A += sm_acc[w][r][d] * e;
+            Ls += sm_ml[w][2 + r] * e;
+        }
+        pp[r * PART + 4 + d] = A;
+        if (d == 0) {
+            pp[r * PART] = M;
+            pp[r * PART + 1] = Ls;
+        }
+    }
+}
+
+// out[b, qh*128 + d] = bf16(combined attention of q head qh): one warp per
+// (q head, sequence); unit maxima are in the log2 domain.
+__global__ void attn_combine_kernel(const float* __restrict__ part, int C, bf16* __restrict__ out, int ld_out) {
+    pdl_wait();
+    pdl_trigger();
+    const int qh = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+    const int h = qh >> 1, hh = qh & 1;
+    const float* base = part + (((size_t)b * 8 + h) * C) * 2 * PART + hh * PART;
+    float M = -INFINITY;
+    for (int c = lane; c < C; c += 32) M = fmaxf(M, base[(size_t)c * 2 * PART]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = 0; c < C; ++c) {
+        const float* pp = base + (size_t)c * 2 * PART;
+        const float m = pp[0];
+        if (m == -INFINITY) continue;
+        const float e = exp2f(m - M);
+        Ls += pp[1] * e;
+        const float4 av = *reinterpret_cast<const float4*>(pp + 4 + 4 * lane);
+        A[0] += av.x * e; A[1] += av.y * e; A[2] += av.z * e; A[3] += av.w * e;
+    }
+    const float inv = 1.f / Ls;
+    bf16* o = out + (size_t)b * ld_out + qh * D + 4 * lane;
+    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(A[0] * inv, A[1] * inv);
+    *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(A[2] * inv, A[3] * inv);
+}
+
+// Blocks [0, norm_blocks): out[r] = bf16(rmsnorm(X[r]) * w), one warp per row
+// (the prefill RMSNorm math).  Remaining blocks zero `zero_n` float4s of the
+// split-K accumulators of this layer's GEMMs.
+__global__ void __launch_bounds__(256) norm_zero_kernel(const float* __restrict__ X, const bf16* __restrict__ w,
+                                                        bf16* __restrict__ out, int rows, int norm_blocks,
+                                                        float4* __restrict__ zero, int zero_n) {
+    pdl_wait();
+    pdl_trigger();
+    if ((int)blockIdx.x >= norm_blocks) {
+        for (int i = (blockIdx.x - norm_blocks) * blockDim.x + threadIdx.x; i < zero_n;
+             i += (gridDim.x - norm_blocks) * blockDim.x)
+            zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        return;
+    }
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (r >= rows) return;
+    const float* x = X + (size_t)r * MQ_HIDDEN_SIZE;
+    float v[32];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int c = (lane + 32 * i) * 8;
+        const float4 a = *reinterpret_cast<const float4*>(x + c);
+        const float4 e = *reinterpret_cast<const float4*>(x + c + 4);
+        v[8 * i + 0] = a.x; v[8 * i + 1] = a.y; v[8 * i + 2] = a.z; v[8 * i + 3] = a.w;
+        v[8 * i + 4] = e.x; v[8 * i + 5] = e.y; v[8 * i + 6] = e.z; v[8 * i + 7] = e.w;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) ss += v[8 * i + k] * v[8 * i + k];
+    }
+    ss = warp_sum(ss);
+    const float rstd = rsqrtf(ss / (float)MQ_HIDDEN_SIZE + 1e-6f);
+    bf16* o = out + (size_t)r * MQ_HIDDEN_SIZE;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int c = (lane + 32 * i) * 8;
+        const uint4 wq = *reinterpret_cast<const uint4*>(w + c);
+        const float wf[8] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y),
+                             bf16lo(wq.z), bf16hi(wq.z), bf16lo(wq.w), bf16hi(wq.w)};
+        uint32_t pk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            __nv_bfloat162 t = __floats2bfloat162_rn(v[8 * i + 2 * k] * rstd * wf[2 * k],
+                                                     v[8 * i + 2 * k + 1] * rstd * wf[2 * k + 1]);
+            pk[k] = *reinterpret_cast<uint32_t*>(&t);
+        }
+        *reinterpret_cast<uint4*>(o + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+}
+
+// X[b] = embed[tokens[b]] (fp32); clears the LM head's argmax keys of this step.
+__global__ void embed_step_kernel(const int* __restrict__ tokens, const bf16* __restrict__ embed,
+                                  float* __restrict__ X, unsigned long long* __restrict__ best, int B) {
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (b >= B) return;
+    if (lane == 0) best[b] = 0ull;
+    const bf16* row = embed + (size_t)tokens[b] * MQ_HIDDEN_SIZE;
+    float* out = X + (size_t)b * MQ_HIDDEN_SIZE;
+#pragma unroll
+    for (int i = 0; i < MQ_HIDDEN_SIZE / 256; ++i) {
+        const int c = (lane + 32 * i) * 8;
+        const uint4 w = *reinterpret_cast<const uint4*>(row + c);
+        *reinterpret_cast<float4*>(out + c) = make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
+        *reinterpret_cast<float4*>(out + c + 4) = make_float4(bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w));
+    }
+}
+
+// tokens[b] = argmax from the LM head's 64-bit keys (value key << 32 | ~index); positions[b] += 1.
+__global__ void finish_step_kernel(const unsigned long long* __restrict__ best, int* __restrict__ tokens,
+                                   int* __restrict__ pos, int B) {
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    tokens[b] = (int)(0xffffffffu - (uint32_t)(best[b] & 0xffffffffull));
+    pos[b] += 1;
+}
+
+// Every kernel of a step is launched as a programmatic dependent of the
+// previous one; each begins with pdl_wait, so stream order still holds.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, ((KArgs)args)...);
+}
+
+struct Layout {
+    size_t X, Xn, QKV, Qf, Kb, Vb, part, attn, act, lastn, best, total;
+};
+
+int np_of(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : B <= 64 ? 64 : 128; }
+
+Layout layout(int B, int max_seq) {
+    const size_t NP = (size_t)np_of(B);
+    const int C = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
+    Layout L;
+    size_t o = 0;
+    auto take = [&](size_t bytes) { size_t r = o; o += (bytes + 1023) & ~size_t(1023); return r; };
+    L.X = take((size_t)B * 1024 * 4);
+    L.Xn = take(NP * 1024 * 2);
+    L.QKV = take((size_t)B * 4096 * 4);
+    L.Qf = take((size_t)B * 2048 * 4);
+    L.Kb = take((size_t)B * 1024 * 2);
+    L.Vb = take((size_t)B * 1024 * 2);
+    L.part = take((size_t)B * 8 * C * 2 * PART * 4);
+    L.attn = take(NP * 2048 * 2);
+    L.act = take(NP * 3072 * 2);
+    L.lastn = take(NP * 1024 * 2);
+    L.best = take((size_t)B * 8);
+    L.total = o;
+    return L;
+}
+
+unsigned long long* g_trace = nullptr;
+int g_launches = 0;   // small GEMM launches so far (all modes), for MQ_SMALL_TRACE
+
+// Deepest ring that fits the 227 KB shared-memory limit of a CTA.
+template <typename Cfg>
+constexpr int fit_stages() {
+    int s = Cfg::MAX_STAGES;
+    while (s > 1 && Cfg::smem_bytes(s) > 232448) --s;
+    return s;
+}
+
+// One small-batch GEMM launch (gemm_small_kernel): up to three weight maps of
+// Nmap[i] rows x K (SM_STORE side by side; SM_SILU: gate, up).  The K split S
+// (the cluster size, <= 8) targets about one CTA per SM.
+template <int MODE>
+int small_gemm(const void* const* W, const int* Nmap, int nmaps, int K, const void* X, int NP, const Small2Args& base,
+               cudaStream_t st) {
+    CUtensorMap tw[3], tx;
+    int tiles[3] = {0, 0, 0}, cols[3] = {0, 0, 0}, total = 0;
+    for (int i = 0; i < 3; ++i) {
+        const int m = i < nmaps ? i : nmaps - 1;
+        if (!make_tmap(&tw[i], W[m], (uint64_t)Nmap[m], (uint64_t)K, (uint64_t)K, GEMM_BM)) return MQ_ERR_CUDA;
+        if (i < nmaps) {
+            tiles[i] = Nmap[i] / GEMM_BM;
+            cols[i] = total * GEMM_BM;
+            total += tiles[i];
+        }
+    }
+    if (MODE == SM_SILU) total = tiles[0];   // gate tile t and up tile t share a CTA
+    if (!make_tmap(&tx, X, (uint64_t)NP, (uint64_t)K, (uint64_t)K, (uint32_t)NP)) return MQ_ERR_CUDA;
+    const int kblocks = K / GEMM_BK;
+    int S = 1;
+    if (MODE != SM_ARGMAX) S = std::max(1, std::min(8, std::min(kblocks, 148 / total)));
+    const int kpb = (kblocks + S - 1) / S;
+    S = (kblocks + kpb - 1) / kpb;
+    Small2Args a = base;
+    a.tiles0 = tiles[0];
+    a.tiles1 = tiles[1];
+    a.col1 = cols[1];
+    a.col2 = cols[2];
+    a.K = K;
+    a.kpb = kpb;
+    a.timeout_cycles = 4000000000ll;
+    a.trace = nullptr;
+    {
+        // phase-timing hook: MQ_SMALL_TRACE=<n> stamps the n-th small GEMM launch of the process
+        static const int trace_at = [] { const char* e = getenv("MQ_SMALL_TRACE"); return e ? atoi(e) : -1; }();
+        if (trace_at >= 0 && g_launches++ == trace_at) {
+            if (!g_trace) cudaMalloc(&g_trace, 8 * 4096 * sizeof(unsigned long long));
+            cudaMemsetAsync(g_trace, 0, 8 * 4096 * sizeof(unsigned long long), st);
+            a.trace = g_trace;
+        }
+    }
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(total, 1, S);
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = S;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    static bool configured[4][64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e;
+    switch (NP) {
+#define MQ_SMALL_CASE(NPV, IDX)                                                                               \
+    case NPV: {                                                                                               \
+        using Cfg = Small2Cfg<NPV, MODE>;                                                                     \
+        if (!configured[IDX][dev & 63]) {                                                                     \
+            const cudaError_t ea = cudaFuncSetAttribute(gemm_small_kernel<NPV, MODE>,                          \
+                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::smem_bytes(fit_stages<Cfg>()));             \
+            if (ea != cudaSuccess) return note_cuda(ea, "small gemm smem attribute");                        \
+            configured[IDX][dev & 63] = true;                                                                 \
+        }                                                                                                     \
+        a.stages = std::min(kpb, MODE == SM_ARGMAX ? 4 : fit_stages<Cfg>());                                  \
+        cfg.dynamicSmemBytes = (size_t)Cfg::smem_bytes(a.stages);                                             \
+        e = cudaLaunchKernelEx(&cfg, gemm_small_kernel<NPV, MODE>, tw[0], tw[1], tw[2], tx, a);               \
+        break;                                                                                                \
+    }
+        MQ_SMALL_CASE(16, 0)
+        MQ_SMALL_CASE(32, 1)
+        MQ_SMALL_CASE(64, 2)
+        MQ_SMALL_CASE(128, 3)
+#undef MQ_SMALL_CASE
+        default: return MQ_ERR_INVALID_ARGUMENT;
+    }
+    return e == cudaSuccess ? MQ_OK : note_cuda(e, "small gemm launch");
+}
+
+}  // namespace db
+
+int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
+    using namespace db;
+    if (!p || !p->tokens || !p->positions || !p->embed || !p->layers_host || !p->final_norm || !p->lm_head ||
+        !p->cos_table || !p->sin_table || !p->k_cache || !p->v_cache || !p->workspace || !p->err_flag)
+        return MQ_ERR_INVALID_ARGUMENT;
+    const int B = p->batch;
+    if (B < 1 || B > 128 || p->num_layers < 1 || p->num_layers > MQ_MAX_LAYERS || p->max_seq_len < 1)
+        return MQ_ERR_INVALID_ARGUMENT;
+    const Layout L = layout(B, p->max_seq_len);
+    if (p->workspace_bytes < L.total) return MQ_ERR_WORKSPACE;
+    uint8_t* ws = (uint8_t*)p->workspace;
+    float* X = (float*)(ws + L.X);
+    bf16* Xn = (bf16*)(ws + L.Xn);
+    float* QKV = (float*)(ws + L.QKV);
+    float* Qf = (float*)(ws + L.Qf);
+    float* part = (float*)(ws + L.part);
+    bf16* attn = (bf16*)(ws + L.attn);
+    bf16* act = (bf16*)(ws + L.act);
+    bf16* lastn = (bf16*)(ws + L.lastn);
+    unsigned long long* best = (unsigned long long*)(ws + L.best);
+    const int NP = np_of(B);
+    const int C = (p->max_context + ATT_CHUNK - 1) / ATT_CHUNK;
+    if (C < 1 || p->max_context > p->max_seq_len) return MQ_ERR_INVALID_ARGUMENT;
+    const int norm_blocks = (B + 7) / 8;
+    const float* cX = X;
+    cudaError_t e = cudaSuccess;
+    auto ok = [&](cudaError_t r) { if (r != cudaSuccess && e == cudaSuccess) e = r; };
+    Small2Args ga = {};
+    ga.Bv = B;
+    ga.err = p->err_flag;
+
+    ok(launch(embed_step_kernel, dim3(norm_blocks), dim3(256), 0, st, (const int*)p->tokens, (const bf16*)p->embed, X,
+              best, B));
+    for (int l = 0; l < p->num_layers; ++l) {
+        const LDGLayerWeights& W = p->layers_host[l];
+        ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX, (const bf16*)W.input_layernorm_weight,
+                  Xn, B, norm_blocks, (float4*)nullptr, 0));
+        const void* wqkv[3] = {W.q_proj_weight, W.k_proj_weight, W.v_proj_weight};
+        const int nqkv[3] = {2048, 1024, 1024};
+        Small2Args a = ga;
+        a.out = QKV;
+        a.ldo = 4096;
+        int rc = small_gemm<SM_STORE>(wqkv, nqkv, 3, 1024, Xn, NP, a, st);
+        if (rc) return rc;
+        pf::QkvArgs qa;
+        qa.qkv = QKV;
+        qa.q_norm = (const bf16*)W.q_norm_weight;
+        qa.k_norm = (const bf16*)W.k_norm_weight;
+        qa.cos_table = (const bf16*)p->cos_table;
+        qa.sin_table = (const bf16*)p->sin_table;
+        qa.Qb = nullptr;
+        qa.Kb = (bf16*)(ws + L.Kb);
+        qa.Vb = (bf16*)(ws + L.Vb);
+        const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * D;
+        qa.k_cache = (bf16*)p->k_cache + layer_off;
+        qa.v_cache = (bf16*)p->v_cache + layer_off;
+        qa.cache_seq_stride = p->cache_seq_stride;
+        qa.S = 1;
+        qa.start_pos = 0;
+        qa.max_seq_len = p->max_seq_len;
+        qa.pos_dev = p->positions;
+        qa.Qf = Qf;
+        ok(launch(pf::qknorm_rope_kernel, dim3(B), dim3(1024), 0, st, qa));
+        ok(launch(attn_unit_kernel, dim3(C, 8, B), dim3(128), 0, st, (const float*)Qf, (const bf16*)qa.k_cache,
+                  (const bf16*)qa.v_cache, (const int*)p->positions, p->cache_seq_stride, p->max_seq_len, C,
+                  p->attn_scale * 1.4426950408889634f, part));
+        ok(launch(attn_combine_kernel, dim3(16, B), dim3(32), 0, st, (const float*)part, C, attn, 2048));
+        const void* wo[1] = {W.o_proj_weight};
+        const int no[1] = {1024};
+        a = ga;
+        a.out = X;
+        a.ldo = 1024;
+        rc = small_gemm<SM_RESID>(wo, no, 1, 2048, attn, NP, a, st);
+        if (rc) return rc;
+        ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX,
+                  (const bf16*)W.post_attn_layernorm_weight, Xn, B, norm_blocks, (float4*)nullptr, 0));
+        const void* wgu[2] = {W.gate_proj_weight, W.up_proj_weight};
+        const int ngu[2] = {3072, 3072};
+        a = ga;
+        a.act = act;
+        a.ldo = 3072;
+        rc = small_gemm<SM_SILU>(wgu, ngu, 2, 1024, Xn, NP, a, st);
+        if (rc) return rc;
+        const void* wd[1] = {W.down_proj_weight};
+        const int nd[1] = {1024};
+        a = ga;
+        a.out = X;
+        a.ldo = 1024;
+        rc = small_gemm<SM_RESID>(wd, nd, 1, 3072, act, NP, a, st);
+        if (rc) return rc;
+    }
+    ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX, (const bf16*)p->final_norm, lastn, B,
+              norm_blocks, (float4*)nullptr, 0));
+    const void* wl[1] = {p->lm_head};
+    const int nl[1] = {MQ_VOCAB_SIZE};
+    Small2Args a = ga;
+    a.out = p->logits;
+    a.ldo = MQ_VOCAB_SIZE;
+    a.best = best;
+    int rc = small_gemm<SM_ARGMAX>(wl, nl, 1, 1024, lastn, NP, a, st);
+    if (rc) return rc;
+    ok(launch(finish_step_kernel, dim3((B + 127) / 128), dim3(128), 0, st, (const unsigned long long*)best, p->tokens,
+              p->positions, B));
+    if (e != cudaSuccess) return note_cuda(e, "batch decode launch");
+    e = cudaGetLastError();
+    return e == cudaSuccess ? MQ_OK : note_cuda(e, "batch decode");
+}
+
+size_t decode_batch_workspace_bytes(int batch, int max_seq_len) { return db::layout(batch, max_seq_len).total; }
+
+}  // namespace mq
+
+extern "C" {
+
+size_t mq_decode_batch_workspace_bytes(int batch, int max_seq_len) {
+    return mq::decode_batch_workspace_bytes(batch, max_seq_len);
+}
+
+// Copies the phase stamps of the traced small GEMM launch (MQ_SMALL_TRACE) to host.
+int mq_debug_small_trace(unsigned long long* host, int n) {
+    if (!mq::db::g_trace) return 0;
+    cudaMemcpy(host, mq::db::g_trace, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    return n;
+}
+
+int mq_decode_batch(const mq_decode_batch_params* params, cudaStream_t stream) {
+    return mq::decode_batch(params, stream);
+}
+
+}  // extern "C"

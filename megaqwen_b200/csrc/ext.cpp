@@ -15,6 +15,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
+#include <algorithm>
 #include <cmath>
 #include <stdexcept>
 #include <string>
@@ -580,6 +581,185 @@ std::tuple<int, torch::Tensor> decode_ldg_with_logits(
 
 }  // namespace
 
+
+// ---------------------------------------------------------------------------
+// Batched greedy decode (config 5 serving path): `batch` independent
+// sequences, each with its own cache [L, 8, max_seq_len, 128] and position.
+// step() launches one decode step for all of them without a host sync; with
+// use_graph the step is captured once per attention-context bucket (chunks of
+// 256 positions, doubled) and replayed.
+class MegakernelBatchDecoder {
+public:
+    MegakernelBatchDecoder(torch::Tensor embed_weight, std::vector<torch::Tensor> layer_weights_flat,
+                           torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+                           torch::Tensor sin_table, int num_layers, int max_seq_len, int batch, bool use_graph)
+        : num_layers_(num_layers), max_seq_len_(max_seq_len), batch_(batch), use_graph_(use_graph) {
+        if (num_layers < 1 || num_layers > MQ_MAX_LAYERS) throw std::runtime_error("num_layers out of range");
+        if (batch < 1 || batch > 128) throw std::runtime_error("batch must be in [1, 128]");
+        if ((int)layer_weights_flat.size() != num_layers * 11)
+            throw std::runtime_error("layer_weights_flat must hold num_layers * 11 tensors");
+        check_bf16(embed_weight, "embed_weight", {kVocab, kHidden});
+        check_bf16(final_norm_weight, "final_norm_weight", {kHidden});
+        check_bf16(lm_head_weight, "lm_head_weight", {kVocab, kHidden});
+        for (int i = 0; i < num_layers * 11; ++i)
+            check_bf16(layer_weights_flat[i], kLayerNames[i % 11], layer_shape(i % 11));
+        if (cos_table.dim() != 2 || cos_table.size(0) < max_seq_len || sin_table.sizes() != cos_table.sizes())
+            throw std::runtime_error("cos/sin tables must be [>=max_seq_len, 128]");
+        device_ = embed_weight.device();
+        c10::cuda::CUDAGuard guard(device_);
+        keep_ = layer_weights_flat;
+        keep_.push_back(embed_weight);
+        keep_.push_back(final_norm_weight);
+        keep_.push_back(lm_head_weight);
+        keep_.push_back(cos_table);
+        keep_.push_back(sin_table);
+        host_.resize(num_layers);
+        for (int i = 0; i < num_layers; ++i) host_[i] = make_layer(layer_weights_flat, (size_t)i * 11);
+        auto bf = torch::dtype(torch::kBFloat16).device(device_);
+        auto i32 = torch::dtype(torch::kInt32).device(device_);
+        k_cache_ = torch::zeros({batch, num_layers, MQ_NUM_KV_HEADS, max_seq_len, MQ_HEAD_DIM}, bf);
+        v_cache_ = torch::zeros_like(k_cache_);
+        tokens_ = torch::zeros({batch}, i32);
+        positions_ = torch::zeros({batch}, i32);
+        err_ = torch::zeros({1}, i32);
+        logits_ = torch::empty({batch, kVocab}, torch::dtype(torch::kFloat32).device(device_));
+        ws_ = torch::empty({(int64_t)mq_decode_batch_workspace_bytes(batch, max_seq_len)},
+                           torch::dtype(torch::kUInt8).device(device_));
+        p_ = {};
+        p_.tokens = tokens_.data_ptr<int>();
+        p_.positions = positions_.data_ptr<int>();
+        p_.batch = batch;
+        p_.embed = embed_weight.data_ptr();
+        p_.layers_host = host_.data();
+        p_.final_norm = final_norm_weight.data_ptr();
+        p_.lm_head = lm_head_weight.data_ptr();
+        p_.cos_table = cos_table.data_ptr();
+        p_.sin_table = sin_table.data_ptr();
+        p_.k_cache = k_cache_.data_ptr();
+        p_.v_cache = v_cache_.data_ptr();
+        p_.cache_seq_stride = (long long)num_layers * MQ_NUM_KV_HEADS * max_seq_len * MQ_HEAD_DIM;
+        p_.num_layers = num_layers;
+        p_.max_seq_len = max_seq_len;
+        p_.attn_scale = 1.0f / sqrtf(128.0f);
+        p_.workspace = ws_.data_ptr();
+        p_.workspace_bytes = (size_t)ws_.numel();
+        p_.err_flag = err_.data_ptr<int>();
+    }
+    ~MegakernelBatchDecoder() {
+        drop_graph();
+        if (cap_stream_) cudaStreamDestroy(cap_stream_);
+    }
+
+    // tokens / positions: int [batch] (any device); position b must be < max_seq_len.
+    void set_state(torch::Tensor tokens, torch::Tensor positions) {
+        auto t = tokens.to(torch::kInt32).cpu().contiguous();
+        auto q = positions.to(torch::kInt32).cpu().contiguous();
+        if (t.numel() != batch_ || q.numel() != batch_) throw std::runtime_error("tokens/positions must have batch entries");
+        int mx = 0;
+        for (int b = 0; b < batch_; ++b) {
+            const int tk = t.data_ptr<int>()[b], ps = q.data_ptr<int>()[b];
+            if (tk < 0 || tk >= kVocab) throw std::runtime_error("token out of range");
+            if (ps < 0 || ps >= max_seq_len_) throw std::runtime_error("position out of range");
+            mx = std::max(mx, ps);
+        }
+        c10::cuda::CUDAGuard guard(device_);
+        tokens_.copy_(t);
+        positions_.copy_(q);
+        max_pos_ = mx;
+    }
+
+    // One step for all sequences; returns the device token tensor (updated in place).
+    torch::Tensor step(bool with_logits) {
+        if (max_pos_ >= max_seq_len_) throw std::runtime_error("position exceeds max_seq_len");
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t st = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
+        const int chunks = (max_pos_ + 1 + 255) / 256;
+        int bucket = 1;
+        while (bucket < chunks) bucket *= 2;
+        const int ctx = std::min(bucket * 256, max_seq_len_);
+        p_.max_context = ctx;
+        p_.logits = with_logits ? logits_.data_ptr<float>() : nullptr;
+        if (!use_graph_ || with_logits) {
+            const int rc = mq_decode_batch(&p_, st);
+            if (rc) raise_engine(rc, 0, "batch step");
+        } else {
+            if (!graph_exec_ || graph_ctx_ != ctx || graph_stream_ != st) {
+                drop_graph();
+                // one eager step before capture configures the kernels (attributes are not graph nodes)
+                if (!warmed_) {
+                    const int rc = mq_decode_batch(&p_, st);
+                    if (rc) raise_engine(rc, 0, "batch step");
+                    warmed_ = true;
+                    ++max_pos_;
+                    return tokens_;
+                }
+                // captured on a private stream (the legacy default stream cannot be captured)
+                if (!cap_stream_ && cudaStreamCreateWithFlags(&cap_stream_, cudaStreamNonBlocking) != cudaSuccess)
+                    throw std::runtime_error("cudaStreamCreateWithFlags failed");
+                cudaGraph_t g = nullptr;
+                if (cudaStreamBeginCapture(cap_stream_, cudaStreamCaptureModeThreadLocal) != cudaSuccess)
+                    throw std::runtime_error("cudaStreamBeginCapture failed");
+                const int rc = mq_decode_batch(&p_, cap_stream_);
+                const cudaError_t ce = cudaStreamEndCapture(cap_stream_, &g);
+                if (rc || ce != cudaSuccess) {
+                    if (g) cudaGraphDestroy(g);
+                    raise_engine(rc ? rc : MQ_ERR_CUDA, 0, "batch step capture");
+                }
+                if (cudaGraphInstantiate(&graph_exec_, g, 0) != cudaSuccess) {
+                    cudaGraphDestroy(g);
+                    graph_exec_ = nullptr;
+                    throw std::runtime_error("cudaGraphInstantiate failed");
+                }
+                cudaGraphDestroy(g);
+                graph_ctx_ = ctx;
+                graph_stream_ = st;
+            }
+            if (cudaGraphLaunch(graph_exec_, st) != cudaSuccess) throw std::runtime_error("cudaGraphLaunch failed");
+        }
+        ++max_pos_;
+        return tokens_;
+    }
+
+    // Runs n steps and returns the generated tokens [n, batch] (device).
+    torch::Tensor generate(int n) {
+        c10::cuda::CUDAGuard guard(device_);
+        auto out = torch::empty({n, batch_}, tokens_.options());
+        for (int i = 0; i < n; ++i) out[i].copy_(step(false), true);
+        return out;
+    }
+
+    // Raises if a device wait ran out (synchronises).
+    void check() {
+        c10::cuda::CUDAGuard guard(device_);
+        const int e = err_.cpu().item<int>();
+        if (e) raise_engine(MQ_ERR_PIPE_TIMEOUT, (uint32_t)e, "batch decode");
+    }
+
+    torch::Tensor tokens() { return tokens_; }
+    torch::Tensor positions() { return positions_; }
+    torch::Tensor logits() { return logits_; }
+    torch::Tensor get_k_cache() { return k_cache_; }
+    torch::Tensor get_v_cache() { return v_cache_; }
+    int batch() const { return batch_; }
+    int64_t workspace_bytes() const { return ws_.numel(); }
+
+private:
+    void drop_graph() {
+        if (graph_exec_) cudaGraphExecDestroy(graph_exec_);
+        graph_exec_ = nullptr;
+    }
+    int num_layers_, max_seq_len_, batch_;
+    bool use_graph_, warmed_ = false;
+    int max_pos_ = 0, graph_ctx_ = 0;
+    cudaStream_t graph_stream_ = nullptr, cap_stream_ = nullptr;
+    cudaGraphExec_t graph_exec_ = nullptr;
+    torch::Device device_{torch::kCPU};
+    std::vector<torch::Tensor> keep_;
+    std::vector<LDGLayerWeights> host_;
+    torch::Tensor k_cache_, v_cache_, tokens_, positions_, err_, logits_, ws_;
+    mq_decode_batch_params p_;
+};
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.doc() = "B200 (sm_100a) Qwen3-0.6B decode engine: reference-compatible torch extension";
     py::class_<MegakernelDecoder>(m, "MegakernelDecoder")
@@ -623,6 +803,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
              py::arg("embed_weight"), py::arg("layer_weights_flat"), py::arg("final_norm_weight"),
              py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
              py::arg("max_seq_len"), py::arg("max_prefill_len") = 64);
+    py::class_<MegakernelBatchDecoder>(m, "MegakernelBatchDecoder")
+        .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
+                      torch::Tensor, int, int, int, bool>(),
+             py::arg("embed_weight"), py::arg("layer_weights_flat"), py::arg("final_norm_weight"),
+             py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
+             py::arg("max_seq_len"), py::arg("batch"), py::arg("use_graph") = true)
+        .def("set_state", &MegakernelBatchDecoder::set_state)
+        .def("step", &MegakernelBatchDecoder::step, py::arg("with_logits") = false)
+        .def("generate", &MegakernelBatchDecoder::generate)
+        .def("check", &MegakernelBatchDecoder::check)
+        .def("tokens", &MegakernelBatchDecoder::tokens)
+        .def("positions", &MegakernelBatchDecoder::positions)
+        .def("logits", &MegakernelBatchDecoder::logits)
+        .def("get_k_cache", &MegakernelBatchDecoder::get_k_cache)
+        .def("get_v_cache", &MegakernelBatchDecoder::get_v_cache)
+        .def("batch", &MegakernelBatchDecoder::batch)
+        .def("workspace_bytes", &MegakernelBatchDecoder::workspace_bytes);
     m.def("init_ldg_layer_weights", &init_ldg_layer_weights);
     m.def("init_ldg_embed_weight", &init_ldg_embed_weight);
     m.def("decode_ldg", &decode_ldg);

@@ -205,3 +205,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 }
 
 }  // namespace mq
+
+namespace mq {
+
+}  // namespace mq

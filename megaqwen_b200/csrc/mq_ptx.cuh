@@ -121,6 +121,14 @@ __device__ __forceinline__ bool named_bar_or(uint32_t id, uint32_t nthreads, boo
     return r != 0;
 }
 
+// ---- programmatic dependent launch ----------------------------------------------
+// Both are no-ops for a kernel launched without the programmatic-serialization
+// attribute.  pdl_wait: this thread waits until the stream predecessor grid has
+// completed and its writes are visible.  pdl_trigger: this CTA allows the
+// stream successor to be scheduled (it still waits in its own pdl_wait).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- bf16 unpacking -----------------------------------------------------------
 __device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }

@@ -30,17 +30,21 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 // K-major bf16 matrix [rows, cols] with row stride ld (elements); box 64 x 128,
 // 128-byte swizzle (matches sw128_kmajor_desc).
-bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld) {
+}  // namespace
+
+bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld * 2};
-    cuuint32_t box[2] = {GEMM_BK, GEMM_BM};
+    cuuint32_t box[2] = {GEMM_BK, box_rows};
     cuuint32_t estr[2] = {1, 1};
     return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+namespace {
 
 template <int EPI>
 int launch_gemm(const void* A, int lda, const void* B, int ldb, const void* B2, void* C, int ldc, int M, int N,
@@ -56,10 +60,10 @@ int launch_gemm(const void* A, int lda, const void* B, int ldb, const void* B2, 
         configured[dev] = true;
     }
     CUtensorMap ta, tb, tb2;
-    if (!make_tmap(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda)) return MQ_ERR_CUDA;
-    if (!make_tmap(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb)) return MQ_ERR_CUDA;
+    if (!make_tmap(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, GEMM_BM)) return MQ_ERR_CUDA;
+    if (!make_tmap(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, GEMM_BN)) return MQ_ERR_CUDA;
     tb2 = tb;
-    if (EPI == EPI_SILU_MUL && !make_tmap(&tb2, B2, (uint64_t)N, (uint64_t)K, (uint64_t)ldb)) return MQ_ERR_CUDA;
+    if (EPI == EPI_SILU_MUL && !make_tmap(&tb2, B2, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, GEMM_BN)) return MQ_ERR_CUDA;
     GemmArgs a;
     a.C = C;
     a.ldc = ldc;
@@ -200,6 +204,8 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
         qa.S = S;
         qa.start_pos = 0;
         qa.max_seq_len = p->max_seq_len;
+        qa.pos_dev = nullptr;
+        qa.Qf = nullptr;
         pf::qknorm_rope_kernel<<<M, 1024, 0, st>>>(qa);
         dim3 fgrid((S + pf::FA_B - 1) / pf::FA_B, MQ_NUM_Q_HEADS, B);
         pf::flash_attn_causal_kernel<<<fgrid, 128, pf::FA_SMEM, st>>>(Qb, Kb, Vb, Ob, S, scale_log2);

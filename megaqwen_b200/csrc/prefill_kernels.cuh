@@ -2,6 +2,9 @@
 // QK-norm + RoPE + K/V cache write, causal GQA flash attention on the tensor
 // cores (mma.sync m16n8k16 bf16 -> fp32), and argmax.
 //
+// The kernels begin with pdl_wait/pdl_trigger so that the batched decode can
+// launch them as programmatic dependents (no-ops in an ordinary launch).
+//
 // Activation layout: rows m = b * S + s (sequence b, position s), row-major.
 // Residual stream X fp32 [M, 1024]; GEMM operands bf16.
 #pragma once
@@ -24,8 +27,10 @@ constexpr int NQ = MQ_NUM_Q_HEADS;
 constexpr int NKV = MQ_NUM_KV_HEADS;
 
 // X[m, :] = embed[ids[m], :] (fp32).  One warp per row.
-__global__ void embed_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed, float* __restrict__ X,
+static __global__ void embed_kernel(const int* __restrict__ ids, const bf16* __restrict__ embed, float* __restrict__ X,
                              int M) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (m >= M) return;
@@ -42,8 +47,10 @@ __global__ void embed_kernel(const int* __restrict__ ids, const bf16* __restrict
 
 // out[r, :] = bf16(x * rsqrt(mean(x^2) + eps) * w) with x = X[r * in_stride + in_offset, :].
 // One warp per output row (demo_e2e.py:37-53 math, fp32).
-__global__ void rmsnorm_bf16_kernel(const float* __restrict__ X, const bf16* __restrict__ w, bf16* __restrict__ out,
+static __global__ void rmsnorm_bf16_kernel(const float* __restrict__ X, const bf16* __restrict__ w, bf16* __restrict__ out,
                                     int rows, int in_stride, int in_offset) {
+    pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
     if (r >= rows) return;
@@ -98,12 +105,16 @@ struct QkvArgs {
     bf16* v_cache;
     long long cache_seq_stride;  // elements between sequences' caches
     int S, start_pos, max_seq_len;
+    const int* pos_dev;      // optional: position of sequence b is pos_dev[b] (batched decode, S == 1)
+    float* Qf;               // optional: fp32 q [M, 2048] instead of bf16 Qb
 };
 
-__global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkvArgs a) {
+static __global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkvArgs a) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = m / a.S, p = a.start_pos + (m - b * a.S);
+    const int b = m / a.S, p = a.pos_dev ? a.pos_dev[b] : a.start_pos + (m - b * a.S);
     const float* row = a.qkv + (size_t)m * 4096;
     float e[4];
     if (warp < NQ + NKV) {
@@ -126,7 +137,10 @@ __global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkvArgs a) {
             const float c = __bfloat162float(cs[i]), s = __bfloat162float(sn[i]);
             o[j] = (j < 2) ? (e[j] * c - e[j + 2] * s) : (e[j] * c + e[j - 2] * s);
         }
-        if (isq) {
+        if (isq && a.Qf) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) a.Qf[(size_t)m * 2048 + warp * D + lane + 32 * j] = o[j];
+        } else if (isq) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) a.Qb[(size_t)m * 2048 + warp * D + lane + 32 * j] = __float2bfloat16(o[j]);
         } else {
@@ -153,8 +167,10 @@ __global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkvArgs a) {
 }
 
 // tokens[r] = lowest index of the maximum of logits[r, :V]; logits_ld elements per row.
-__global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int logits_ld,
+static __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int logits_ld,
                                                       int* __restrict__ tokens) {
+    pdl_wait();
+    pdl_trigger();
     const float* x = logits + (size_t)blockIdx.x * logits_ld;
     float best = -INFINITY;
     int bi = 0x7fffffff;
