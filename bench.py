@@ -323,6 +323,42 @@ def run_ours(args, rank, world, local):
     else:
         sweep_prefill = None
 
+    # --- batched decode (config 5): B independent sequences per GPU, one token each per step ---
+    batch = {}
+    if args.batch_sizes:
+        g = torch.Generator(device=dev).manual_seed(13)
+        for B in args.batch_sizes:
+            for P in (16, 1024):
+                MS = P + args.batch_steps + 16
+                bd = megaqwen_b200._C.MegakernelBatchDecoder(w.embed, w.layer_weights_flat(), w.final_norm,
+                                                             w.lm_head, cos, sin, 28, MS, B, True)
+                kc, vc = bd.get_k_cache(), bd.get_v_cache()
+                kc[:, :, :, :P].normal_(generator=g)
+                vc[:, :, :, :P].normal_(generator=g)
+                bd.set_state(torch.arange(B) * 37 + 5, torch.full((B,), P))
+                for _ in range(3):
+                    bd.step(False)
+                torch.cuda.synchronize()
+                barrier(world)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                n = args.batch_steps
+                e0.record()
+                for _ in range(n):
+                    bd.step(False)
+                e1.record()
+                torch.cuda.synchronize()
+                bd.check()
+                ms = max_over_ranks(e0.elapsed_time(e1), world) / n
+                pm = P + 3 + n // 2
+                step_bytes = WEIGHT_BYTES + B * KV_BYTES_PER_POS * (pm + 2)
+                batch[f"B{B}_pos{P}"] = {
+                    "tok_s": round(world * B / (ms / 1000.0), 1), "tok_s_per_gpu": round(B / (ms / 1000.0), 1),
+                    "ms_per_step": round(ms, 4),
+                    "roofline_frac": round(step_bytes / (ms / 1000.0) / 1e9 / hbm, 4),
+                    "bytes_per_step": step_bytes}
+                del bd, kc, vc
+                torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, cores, last = cpu_oracle_rate(args.cpu_budget)
@@ -350,6 +386,7 @@ def run_ours(args, rank, world, local):
             "clocks": clk.summary(),
             "positions": sweep,
             "prefill": sweep_prefill,
+            "batch_decode": batch or None,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -364,6 +401,8 @@ def main():
     ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 128, 512, 2048, 8192])
     ap.add_argument("--sweep-steps", type=int, default=64)
     ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--batch-sizes", type=lambda s: [int(x) for x in s.split(",") if x], default=[16, 64])
+    ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     args = ap.parse_args()

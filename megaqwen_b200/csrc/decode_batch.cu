@@ -10,8 +10,10 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdio>
 #include <cstdlib>
 #include <mutex>
+#include <vector>
 
 #include "gemm_small.cuh"
 #include "megaqwen_b200.h"
@@ -58,9 +60,11 @@ __device__ __forceinline__ int vdim(int u, int r, int g) { return 32 * u + 8 * (
 __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict__ Qf, const bf16* __restrict__ kc,
                                                         const bf16* __restrict__ vc, const int* __restrict__ pos,
                                                         long long seq_stride, int max_seq, int C, float scale_log2,
-                                                        float* __restrict__ part) {
+                                                        float* __restrict__ part, int* __restrict__ counters,
+                                                        bf16* __restrict__ out) {
     __shared__ float sm_ml[4][4];
     __shared__ float sm_acc[4][2][D];
+    __shared__ int s_last;
     pdl_wait();
     pdl_trigger();
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -208,6 +212,8 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
     }
     __syncthreads();
     const int d = threadIdx.x;
+    const int nact = (L + ATT_CHUNK - 1) / ATT_CHUNK;   // chunks holding positions of this sequence
+    bf16* o = out + (size_t)b * 2048 + (2 * h) * D + d;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
         float M = -INFINITY;
@@ -221,40 +227,39 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
             A += sm_acc[w][r][d] * e;
             Ls += sm_ml[w][2 + r] * e;
         }
-        pp[r * PART + 4 + d] = A;
-        if (d == 0) {
-            pp[r * PART] = M;
-            pp[r * PART + 1] = Ls;
+        if (nact == 1) {
+            o[r * D] = __float2bfloat16(A / Ls);
+        } else {
+            pp[r * PART + 4 + d] = A;
+            if (d == 0) {
+                pp[r * PART] = M;
+                pp[r * PART + 1] = Ls;
+            }
         }
     }
-}
-
-// out[b, qh*128 + d] = bf16(combined attention of q head qh): one warp per
-// (q head, sequence); unit maxima are in the log2 domain.
-__global__ void attn_combine_kernel(const float* __restrict__ part, int C, bf16* __restrict__ out, int ld_out) {
-    pdl_wait();
-    pdl_trigger();
-    const int qh = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
-    const int h = qh >> 1, hh = qh & 1;
-    const float* base = part + (((size_t)b * 8 + h) * C) * 2 * PART + hh * PART;
-    float M = -INFINITY;
-    for (int c = lane; c < C; c += 32) M = fmaxf(M, base[(size_t)c * 2 * PART]);
+    if (nact == 1) return;
+    // the last unit of (sequence, kv head) to finish merges all chunks
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = atomicAdd(counters + b * 8 + h, 1) == nact - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) counters[b * 8 + h] = 0;   // ready for the next layer
+    const float* base = part + (((size_t)b * 8 + h) * C) * 2 * PART;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    float Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int c = 0; c < C; ++c) {
-        const float* pp = base + (size_t)c * 2 * PART;
-        const float m = pp[0];
-        if (m == -INFINITY) continue;
-        const float e = exp2f(m - M);
-        Ls += pp[1] * e;
-        const float4 av = *reinterpret_cast<const float4*>(pp + 4 + 4 * lane);
-        A[0] += av.x * e; A[1] += av.y * e; A[2] += av.z * e; A[3] += av.w * e;
+    for (int r = 0; r < 2; ++r) {
+        float M = -INFINITY;
+        for (int cc = 0; cc < nact; ++cc) M = fmaxf(M, __ldcg(base + (size_t)cc * 2 * PART + r * PART));
+        float A = 0.f, Ls = 0.f;
+        for (int cc = 0; cc < nact; ++cc) {
+            const float* q = base + (size_t)cc * 2 * PART + r * PART;
+            const float e = exp2f(__ldcg(q) - M);
+            Ls += __ldcg(q + 1) * e;
+            A += __ldcg(q + 4 + d) * e;
+        }
+        o[r * D] = __float2bfloat16(A / Ls);
     }
-    const float inv = 1.f / Ls;
-    bf16* o = out + (size_t)b * ld_out + qh * D + 4 * lane;
-    *reinterpret_cast<__nv_bfloat162*>(o) = __floats2bfloat162_rn(A[0] * inv, A[1] * inv);
-    *reinterpret_cast<__nv_bfloat162*>(o + 2) = __floats2bfloat162_rn(A[2] * inv, A[3] * inv);
 }
 
 // Blocks [0, norm_blocks): out[r] = bf16(rmsnorm(X[r]) * w), one warp per row
@@ -307,14 +312,17 @@ __global__ void __launch_bounds__(256) norm_zero_kernel(const float* __restrict_
     }
 }
 
-// X[b] = embed[tokens[b]] (fp32); clears the LM head's argmax keys of this step.
+// X[b] = embed[tokens[b]] (fp32); clears the LM head's argmax keys and the
+// attention merge counters of this step.
 __global__ void embed_step_kernel(const int* __restrict__ tokens, const bf16* __restrict__ embed,
-                                  float* __restrict__ X, unsigned long long* __restrict__ best, int B) {
+                                  float* __restrict__ X, unsigned long long* __restrict__ best,
+                                  int* __restrict__ counters, int B) {
     pdl_wait();
     pdl_trigger();
     const int b = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
     if (lane == 0) best[b] = 0ull;
+    if (lane < 8) counters[b * 8 + lane] = 0;
     const bf16* row = embed + (size_t)tokens[b] * MQ_HIDDEN_SIZE;
     float* out = X + (size_t)b * MQ_HIDDEN_SIZE;
 #pragma unroll
@@ -355,7 +363,7 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 }
 
 struct Layout {
-    size_t X, Xn, QKV, Qf, Kb, Vb, part, attn, act, lastn, best, total;
+    size_t X, Xn, Qf, part, cnt, attn, act, lastn, best, total;
 };
 
 int np_of(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : B <= 64 ? 64 : 128; }
@@ -368,11 +376,9 @@ Layout layout(int B, int max_seq) {
     auto take = [&](size_t bytes) { size_t r = o; o += (bytes + 1023) & ~size_t(1023); return r; };
     L.X = take((size_t)B * 1024 * 4);
     L.Xn = take(NP * 1024 * 2);
-    L.QKV = take((size_t)B * 4096 * 4);
     L.Qf = take((size_t)B * 2048 * 4);
-    L.Kb = take((size_t)B * 1024 * 2);
-    L.Vb = take((size_t)B * 1024 * 2);
     L.part = take((size_t)B * 8 * C * 2 * PART * 4);
+    L.cnt = take((size_t)B * 8 * 4);
     L.attn = take(NP * 2048 * 2);
     L.act = take(NP * 3072 * 2);
     L.lastn = take(NP * 1024 * 2);
@@ -395,6 +401,91 @@ constexpr int fit_stages() {
 // One small-batch GEMM launch (gemm_small_kernel): up to three weight maps of
 // Nmap[i] rows x K (SM_STORE side by side; SM_SILU: gate, up).  The K split S
 // (the cluster size, <= 8) targets about one CTA per SM.
+// Cluster size (K split) and ring depth per GEMM shape, chosen once per
+// device from the occupancy calculator: the largest split whose clusters all
+// fit in one wave, up to about two CTAs per SM.
+struct SplitChoice {
+    int dev, mode, np, total, kblocks;
+    int S, kpb, stages;
+};
+std::mutex g_split_mu;
+std::vector<SplitChoice> g_splits;
+
+template <int NPV, int MODE>
+int launch_small(int total, int kblocks, Small2Args a, const CUtensorMap* tw, const CUtensorMap& tx, cudaStream_t st) {
+    using Cfg = Small2Cfg<NPV, MODE>;
+    auto kernel = gemm_small_kernel<NPV, MODE>;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = MODE == SM_ARGMAX ? 1 : 2;
+
+    SplitChoice ch = {dev, MODE, NPV, total, kblocks, 1, kblocks, std::min(kblocks, 4)};
+    bool found = false;
+    {
+        std::lock_guard<std::mutex> lk(g_split_mu);
+        for (const SplitChoice& c : g_splits)
+            if (c.dev == dev && c.mode == MODE && c.np == NPV && c.total == total && c.kblocks == kblocks) {
+                ch = c;
+                found = true;
+                break;
+            }
+    }
+    if (!found) {
+        cudaError_t ea = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              Cfg::smem_bytes(fit_stages<Cfg>()));
+        if (ea != cudaSuccess) return note_cuda(ea, "small gemm smem attribute");
+        if (MODE != SM_ARGMAX) {
+            ea = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+            const int cands[] = {16, 12, 8, 6, 4, 3, 2, 1};
+            for (int S : cands) {
+                if (S > kblocks || (ea != cudaSuccess && S > 8)) continue;
+                const int kpb = (kblocks + S - 1) / S;
+                if ((kblocks + kpb - 1) / kpb != S || total * S > 320) continue;
+                const int stages = std::min(kpb, fit_stages<Cfg>());
+                cfg.gridDim = dim3(total, 1, S);
+                cfg.dynamicSmemBytes = (size_t)Cfg::smem_bytes(stages);
+                attr[1].val.clusterDim.z = S;
+                int nclusters = 0;
+                if (cudaOccupancyMaxActiveClusters(&nclusters, kernel, &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    continue;
+                }
+                if (nclusters >= total || S == 1) {
+                    ch.S = S;
+                    ch.kpb = kpb;
+                    ch.stages = stages;
+                    break;
+                }
+            }
+        }
+        if (getenv("MQ_SPLIT_VERBOSE"))
+            fprintf(stderr, "small gemm mode %d NP %d tiles %d kblocks %d -> S %d kpb %d stages %d\n", MODE, NPV,
+                    total, kblocks, ch.S, ch.kpb, ch.stages);
+        std::lock_guard<std::mutex> lk(g_split_mu);
+        g_splits.push_back(ch);
+    }
+    a.kpb = ch.kpb;
+    a.stages = ch.stages;
+    cfg.gridDim = dim3(total, 1, ch.S);
+    cfg.dynamicSmemBytes = (size_t)Cfg::smem_bytes(ch.stages);
+    attr[1].val.clusterDim.z = ch.S;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, tw[0], tw[1], tw[2], tx, a);
+    return e == cudaSuccess ? MQ_OK : note_cuda(e, "small gemm launch");
+}
+
+// One small-batch GEMM (gemm_small_kernel): up to three weight maps of
+// Nmap[i] rows x K (side by side for SM_QKV / SM_STORE; gate, up for SM_SILU).
 template <int MODE>
 int small_gemm(const void* const* W, const int* Nmap, int nmaps, int K, const void* X, int NP, const Small2Args& base,
                cudaStream_t st) {
@@ -411,18 +502,12 @@ int small_gemm(const void* const* W, const int* Nmap, int nmaps, int K, const vo
     }
     if (MODE == SM_SILU) total = tiles[0];   // gate tile t and up tile t share a CTA
     if (!make_tmap(&tx, X, (uint64_t)NP, (uint64_t)K, (uint64_t)K, (uint32_t)NP)) return MQ_ERR_CUDA;
-    const int kblocks = K / GEMM_BK;
-    int S = 1;
-    if (MODE != SM_ARGMAX) S = std::max(1, std::min(8, std::min(kblocks, 148 / total)));
-    const int kpb = (kblocks + S - 1) / S;
-    S = (kblocks + kpb - 1) / kpb;
     Small2Args a = base;
     a.tiles0 = tiles[0];
     a.tiles1 = tiles[1];
     a.col1 = cols[1];
     a.col2 = cols[2];
     a.K = K;
-    a.kpb = kpb;
     a.timeout_cycles = 4000000000ll;
     a.trace = nullptr;
     {
@@ -434,47 +519,14 @@ int small_gemm(const void* const* W, const int* Nmap, int nmaps, int K, const vo
             a.trace = g_trace;
         }
     }
-
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(total, 1, S);
-    cfg.blockDim = dim3(GEMM_THREADS);
-    cfg.stream = st;
-    cudaLaunchAttribute attr[2];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = 1;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = S;
-    cfg.attrs = attr;
-    cfg.numAttrs = 2;
-    static bool configured[4][64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaError_t e;
+    const int kblocks = K / GEMM_BK;
     switch (NP) {
-#define MQ_SMALL_CASE(NPV, IDX)                                                                               \
-    case NPV: {                                                                                               \
-        using Cfg = Small2Cfg<NPV, MODE>;                                                                     \
-        if (!configured[IDX][dev & 63]) {                                                                     \
-            const cudaError_t ea = cudaFuncSetAttribute(gemm_small_kernel<NPV, MODE>,                          \
-                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::smem_bytes(fit_stages<Cfg>()));             \
-            if (ea != cudaSuccess) return note_cuda(ea, "small gemm smem attribute");                        \
-            configured[IDX][dev & 63] = true;                                                                 \
-        }                                                                                                     \
-        a.stages = std::min(kpb, MODE == SM_ARGMAX ? 4 : fit_stages<Cfg>());                                  \
-        cfg.dynamicSmemBytes = (size_t)Cfg::smem_bytes(a.stages);                                             \
-        e = cudaLaunchKernelEx(&cfg, gemm_small_kernel<NPV, MODE>, tw[0], tw[1], tw[2], tx, a);               \
-        break;                                                                                                \
-    }
-        MQ_SMALL_CASE(16, 0)
-        MQ_SMALL_CASE(32, 1)
-        MQ_SMALL_CASE(64, 2)
-        MQ_SMALL_CASE(128, 3)
-#undef MQ_SMALL_CASE
+        case 16: return launch_small<16, MODE>(total, kblocks, a, tw, tx, st);
+        case 32: return launch_small<32, MODE>(total, kblocks, a, tw, tx, st);
+        case 64: return launch_small<64, MODE>(total, kblocks, a, tw, tx, st);
+        case 128: return launch_small<128, MODE>(total, kblocks, a, tw, tx, st);
         default: return MQ_ERR_INVALID_ARGUMENT;
     }
-    return e == cudaSuccess ? MQ_OK : note_cuda(e, "small gemm launch");
 }
 
 }  // namespace db
@@ -492,7 +544,6 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)p->workspace;
     float* X = (float*)(ws + L.X);
     bf16* Xn = (bf16*)(ws + L.Xn);
-    float* QKV = (float*)(ws + L.QKV);
     float* Qf = (float*)(ws + L.Qf);
     float* part = (float*)(ws + L.part);
     bf16* attn = (bf16*)(ws + L.attn);
@@ -510,8 +561,9 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
     ga.Bv = B;
     ga.err = p->err_flag;
 
+    int* counters = (int*)(ws + L.cnt);
     ok(launch(embed_step_kernel, dim3(norm_blocks), dim3(256), 0, st, (const int*)p->tokens, (const bf16*)p->embed, X,
-              best, B));
+              best, counters, B));
     for (int l = 0; l < p->num_layers; ++l) {
         const LDGLayerWeights& W = p->layers_host[l];
         ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX, (const bf16*)W.input_layernorm_weight,
@@ -519,33 +571,24 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
         const void* wqkv[3] = {W.q_proj_weight, W.k_proj_weight, W.v_proj_weight};
         const int nqkv[3] = {2048, 1024, 1024};
         Small2Args a = ga;
-        a.out = QKV;
-        a.ldo = 4096;
-        int rc = small_gemm<SM_STORE>(wqkv, nqkv, 3, 1024, Xn, NP, a, st);
-        if (rc) return rc;
-        pf::QkvArgs qa;
-        qa.qkv = QKV;
-        qa.q_norm = (const bf16*)W.q_norm_weight;
-        qa.k_norm = (const bf16*)W.k_norm_weight;
-        qa.cos_table = (const bf16*)p->cos_table;
-        qa.sin_table = (const bf16*)p->sin_table;
-        qa.Qb = nullptr;
-        qa.Kb = (bf16*)(ws + L.Kb);
-        qa.Vb = (bf16*)(ws + L.Vb);
         const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * D;
-        qa.k_cache = (bf16*)p->k_cache + layer_off;
-        qa.v_cache = (bf16*)p->v_cache + layer_off;
-        qa.cache_seq_stride = p->cache_seq_stride;
-        qa.S = 1;
-        qa.start_pos = 0;
-        qa.max_seq_len = p->max_seq_len;
-        qa.pos_dev = p->positions;
-        qa.Qf = Qf;
-        ok(launch(pf::qknorm_rope_kernel, dim3(B), dim3(1024), 0, st, qa));
-        ok(launch(attn_unit_kernel, dim3(C, 8, B), dim3(128), 0, st, (const float*)Qf, (const bf16*)qa.k_cache,
-                  (const bf16*)qa.v_cache, (const int*)p->positions, p->cache_seq_stride, p->max_seq_len, C,
-                  p->attn_scale * 1.4426950408889634f, part));
-        ok(launch(attn_combine_kernel, dim3(16, B), dim3(32), 0, st, (const float*)part, C, attn, 2048));
+        bf16* kc_l = (bf16*)p->k_cache + layer_off;
+        bf16* vc_l = (bf16*)p->v_cache + layer_off;
+        a.qkv.q_norm = (const bf16*)W.q_norm_weight;
+        a.qkv.k_norm = (const bf16*)W.k_norm_weight;
+        a.qkv.cos_table = (const bf16*)p->cos_table;
+        a.qkv.sin_table = (const bf16*)p->sin_table;
+        a.qkv.pos = p->positions;
+        a.qkv.Qf = Qf;
+        a.qkv.k_cache = kc_l;
+        a.qkv.v_cache = vc_l;
+        a.qkv.seq_stride = p->cache_seq_stride;
+        a.qkv.max_seq = p->max_seq_len;
+        int rc = small_gemm<SM_QKV>(wqkv, nqkv, 3, 1024, Xn, NP, a, st);
+        if (rc) return rc;
+        ok(launch(attn_unit_kernel, dim3(C, 8, B), dim3(128), 0, st, (const float*)Qf, (const bf16*)kc_l,
+                  (const bf16*)vc_l, (const int*)p->positions, p->cache_seq_stride, p->max_seq_len, C,
+                  p->attn_scale * 1.4426950408889634f, part, counters, attn));
         const void* wo[1] = {W.o_proj_weight};
         const int no[1] = {1024};
         a = ga;

@@ -6,7 +6,7 @@
 // weight rows (A = W tile, K-major), its N side the NP padded tokens (B = X,
 // K-major), so one tcgen05.mma.kind::f16 (M=128, N=NP, K=16) covers the batch.
 //
-// Grid (tiles, 1, S) in clusters of (1, 1, S): the S CTAs of a cluster split
+// Grid (tiles, 1, S) in clusters of (1, 1, S), S <= 16: the S CTAs of a cluster split
 // the K dimension of one 128-row tile.  Each CTA stages its fp32 partial tile
 // [NP][128] in its own shared memory, and after a cluster barrier CTA r sums
 // the rows (tokens) of slice r across the S partials through distributed
@@ -16,6 +16,7 @@
 //   SM_RESID   out_f32[b, n] += acc                 (residual stream)
 //   SM_SILU    act_bf16[b, n] = silu(acc_gate) * acc_up
 //              (gate and up tiles t in the same CTA: two TMEM accumulators)
+//   SM_QKV     q|k|v heads: QK-RMSNorm + RoPE, q to fp32, k/v rows into the cache
 //   SM_ARGMAX  (S == 1) optional logits store, and per token the largest
 //              value of the tile with its lowest index, merged into a 64-bit
 //              key per token with atomicMax (the LM head's fused argmax)
@@ -35,7 +36,24 @@
 
 namespace mq {
 
-enum SmallMode { SM_STORE = 0, SM_RESID = 1, SM_SILU = 2, SM_ARGMAX = 3 };
+enum SmallMode { SM_STORE = 0, SM_RESID = 1, SM_SILU = 2, SM_ARGMAX = 3, SM_QKV = 4 };
+
+// SM_QKV epilogue operands: the q/k/v projections of one layer, one head per
+// 128-row tile.  q and k heads get RMSNorm over the head (x norm weight) and
+// rotate-half RoPE at the sequence's position; q goes to Qf (fp32), k and v
+// rows (bf16) into the sequence's cache at that position.
+struct QkvEpi {
+    const __nv_bfloat16* q_norm;
+    const __nv_bfloat16* k_norm;
+    const __nv_bfloat16* cos_table;   // [max_seq, 128]
+    const __nv_bfloat16* sin_table;
+    const int* pos;                   // [Bv]
+    float* Qf;                        // [Bv, 2048]
+    __nv_bfloat16* k_cache;           // layer base of sequence 0: [8, max_seq, 128]
+    __nv_bfloat16* v_cache;
+    long long seq_stride;             // elements between sequences' caches
+    int max_seq;
+};
 
 template <int NP, int MODE>
 struct Small2Cfg {
@@ -67,6 +85,7 @@ struct Small2Args {
     int stages;              // ring depth; smem launched as smem_bytes(stages)
     int* err;
     long long timeout_cycles;
+    QkvEpi qkv;              // SM_QKV
     unsigned long long* trace;   // optional: 8 %globaltimer stamps per CTA (phase timing)
 };
 
@@ -121,16 +140,18 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
     float* red = reinterpret_cast<float*>(smem);   // reuses the ring once all MMAs have completed
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    int tile = blockIdx.x, col_off = 0;
+    int tile = blockIdx.x, col_off = 0, map = 0;
     const CUtensorMap* tmA = &tmW0;
-    if (MODE == SM_STORE && tile >= args.tiles0) {
+    if ((MODE == SM_STORE || MODE == SM_QKV) && tile >= args.tiles0) {
         tile -= args.tiles0;
         tmA = &tmW1;
         col_off = args.col1;
+        map = 1;
         if (tile >= args.tiles1) {
             tile -= args.tiles1;
             tmA = &tmW2;
             col_off = args.col2;
+            map = 2;
         }
     }
     const int n0 = tile * GEMM_BM;
@@ -138,6 +159,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
     const int kb0 = blockIdx.z * args.kpb;
     const int nk = max(0, min(args.kpb, args.K / GEMM_BK - kb0));
 
+    const int pre = min(nk, S);
     if (threadIdx.x == 0) {
         trace_stamp(args, 0);
         for (int s = 0; s < S; ++s) {
@@ -147,8 +169,13 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
         mbar_init(accf, 1);
         *abort_flag = 0;
         fence_mbar_init();
-        prefetch_tmap(tmA);
-        if (MODE == SM_SILU) prefetch_tmap(&tmW1);
+        // the weight slices do not depend on the previous kernel: request them first
+        for (int i = 0; i < pre; ++i) {
+            uint8_t* st = smem + i * Cfg::STAGE;
+            mbar_arrive_expect_tx(&full[i], Cfg::STAGE);
+            tma_load_2d(st, tmA, (kb0 + i) * GEMM_BK, n0, &full[i]);
+            if (Cfg::NW == 2) tma_load_2d(st + Cfg::W_BYTES, &tmW1, (kb0 + i) * GEMM_BK, n0, &full[i]);
+        }
         prefetch_tmap(&tmX);
     }
     if (warp == 1) {
@@ -165,13 +192,6 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
 
     if (warp == 0) {
         if (lane == 0) {
-            const int pre = min(nk, S);
-            for (int i = 0; i < pre; ++i) {
-                uint8_t* st = smem + i * Cfg::STAGE;
-                mbar_arrive_expect_tx(&full[i], Cfg::STAGE);
-                tma_load_2d(st, tmA, (kb0 + i) * GEMM_BK, n0, &full[i]);
-                if (MODE == SM_SILU) tma_load_2d(st + Cfg::W_BYTES, &tmW1, (kb0 + i) * GEMM_BK, n0, &full[i]);
-            }
             trace_stamp(args, 1);
             pdl_wait();
             asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -288,19 +308,54 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
 #pragma unroll
             for (int a = 0; a < Cfg::NW; ++a) {
                 const float* loc = red + (a * NP + b) * Cfg::RED_LD + c4;
-                float4 v[8];
+                float4 v[16];
 #pragma unroll
-                for (int q = 0; q < 8; ++q)
+                for (int q = 0; q < 16; ++q)
                     if (q < ksplits) v[q] = ld_dsmem_f32x4(loc, (uint32_t)q);
                 float4 sum = v[0];
 #pragma unroll
-                for (int q = 1; q < 8; ++q)
+                for (int q = 1; q < 16; ++q)
                     if (q < ksplits) {
                         sum.x += v[q].x; sum.y += v[q].y; sum.z += v[q].z; sum.w += v[q].w;
                     }
                 acc[a] = sum;
             }
-            if (MODE == SM_STORE) {
+            if (MODE == SM_QKV) {
+                // one warp = one token row of one head; lane holds dims c4..c4+3
+                const QkvEpi& q = args.qkv;
+                float4 x = acc[0];
+                const int p = q.pos[b];
+                if (map < 2) {
+                    const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+                    const float rs = rsqrtf(ss / (float)GEMM_BM + 1e-6f);
+                    const __nv_bfloat16* nw = (map == 0 ? q.q_norm : q.k_norm) + c4;
+                    x.x = x.x * rs * __bfloat162float(nw[0]);
+                    x.y = x.y * rs * __bfloat162float(nw[1]);
+                    x.z = x.z * rs * __bfloat162float(nw[2]);
+                    x.w = x.w * rs * __bfloat162float(nw[3]);
+                    // rotate-half partner dims (c4 +- 64) live in lane ^ 16
+                    const float y0 = __shfl_xor_sync(0xffffffffu, x.x, 16), y1 = __shfl_xor_sync(0xffffffffu, x.y, 16);
+                    const float y2 = __shfl_xor_sync(0xffffffffu, x.z, 16), y3 = __shfl_xor_sync(0xffffffffu, x.w, 16);
+                    const __nv_bfloat16* cs = q.cos_table + (size_t)p * GEMM_BM + c4;
+                    const __nv_bfloat16* sn = q.sin_table + (size_t)p * GEMM_BM + c4;
+                    const float sg = c4 < 64 ? -1.f : 1.f;
+                    x.x = x.x * __bfloat162float(cs[0]) + sg * y0 * __bfloat162float(sn[0]);
+                    x.y = x.y * __bfloat162float(cs[1]) + sg * y1 * __bfloat162float(sn[1]);
+                    x.z = x.z * __bfloat162float(cs[2]) + sg * y2 * __bfloat162float(sn[2]);
+                    x.w = x.w * __bfloat162float(cs[3]) + sg * y3 * __bfloat162float(sn[3]);
+                }
+                if (map == 0) {
+                    *reinterpret_cast<float4*>(q.Qf + (size_t)b * 2048 + n0 + c4) = x;
+                } else {
+                    __nv_bfloat16* row = (map == 1 ? q.k_cache : q.v_cache) + b * q.seq_stride +
+                                         ((size_t)tile * q.max_seq + p) * GEMM_BM + c4;
+                    const __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y), hi = __floats2bfloat162_rn(x.z, x.w);
+                    uint2 pk;
+                    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+                    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+                    *reinterpret_cast<uint2*>(row) = pk;
+                }
+            } else if (MODE == SM_STORE) {
                 *reinterpret_cast<float4*>(args.out + (size_t)b * args.ldo + col_off + n0 + c4) = acc[0];
             } else if (MODE == SM_RESID) {
                 float4* o = reinterpret_cast<float4*>(args.out + (size_t)b * args.ldo + n0 + c4);
