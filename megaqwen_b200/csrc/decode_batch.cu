@@ -262,60 +262,13 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
     }
 }
 
-// Blocks [0, norm_blocks): out[r] = bf16(rmsnorm(X[r]) * w), one warp per row
-// (the prefill RMSNorm math).  Remaining blocks zero `zero_n` float4s of the
-// split-K accumulators of this layer's GEMMs.
-__global__ void __launch_bounds__(256) norm_zero_kernel(const float* __restrict__ X, const bf16* __restrict__ w,
-                                                        bf16* __restrict__ out, int rows, int norm_blocks,
-                                                        float4* __restrict__ zero, int zero_n) {
-    pdl_wait();
-    pdl_trigger();
-    if ((int)blockIdx.x >= norm_blocks) {
-        for (int i = (blockIdx.x - norm_blocks) * blockDim.x + threadIdx.x; i < zero_n;
-             i += (gridDim.x - norm_blocks) * blockDim.x)
-            zero[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-        return;
-    }
-    const int r = blockIdx.x * 8 + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (r >= rows) return;
-    const float* x = X + (size_t)r * MQ_HIDDEN_SIZE;
-    float v[32];
-    float ss = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = (lane + 32 * i) * 8;
-        const float4 a = *reinterpret_cast<const float4*>(x + c);
-        const float4 e = *reinterpret_cast<const float4*>(x + c + 4);
-        v[8 * i + 0] = a.x; v[8 * i + 1] = a.y; v[8 * i + 2] = a.z; v[8 * i + 3] = a.w;
-        v[8 * i + 4] = e.x; v[8 * i + 5] = e.y; v[8 * i + 6] = e.z; v[8 * i + 7] = e.w;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) ss += v[8 * i + k] * v[8 * i + k];
-    }
-    ss = warp_sum(ss);
-    const float rstd = rsqrtf(ss / (float)MQ_HIDDEN_SIZE + 1e-6f);
-    bf16* o = out + (size_t)r * MQ_HIDDEN_SIZE;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = (lane + 32 * i) * 8;
-        const uint4 wq = *reinterpret_cast<const uint4*>(w + c);
-        const float wf[8] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y),
-                             bf16lo(wq.z), bf16hi(wq.z), bf16lo(wq.w), bf16hi(wq.w)};
-        uint32_t pk[4];
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            __nv_bfloat162 t = __floats2bfloat162_rn(v[8 * i + 2 * k] * rstd * wf[2 * k],
-                                                     v[8 * i + 2 * k + 1] * rstd * wf[2 * k + 1]);
-            pk[k] = *reinterpret_cast<uint32_t*>(&t);
-        }
-        *reinterpret_cast<uint4*>(o + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-}
-
-// X[b] = embed[tokens[b]] (fp32); clears the LM head's argmax keys and the
-// attention merge counters of this step.
+// X[b] = embed[tokens[b]] (fp32), the first GEMM operand Xw[b] = bf16(X[b] * w)
+// (w = layer 0's input RMSNorm weight; the 1/rms scale is applied in the GEMM
+// epilogue) and the per-128-column sums of squares of X[b]; clears the LM
+// head's argmax keys and the attention merge counters of this step.
 __global__ void embed_step_kernel(const int* __restrict__ tokens, const bf16* __restrict__ embed,
-                                  float* __restrict__ X, unsigned long long* __restrict__ best,
+                                  const bf16* __restrict__ w, float* __restrict__ X, bf16* __restrict__ Xw,
+                                  float* __restrict__ ss, unsigned long long* __restrict__ best,
                                   int* __restrict__ counters, int B) {
     pdl_wait();
     pdl_trigger();
@@ -325,12 +278,30 @@ __global__ void embed_step_kernel(const int* __restrict__ tokens, const bf16* __
     if (lane < 8) counters[b * 8 + lane] = 0;
     const bf16* row = embed + (size_t)tokens[b] * MQ_HIDDEN_SIZE;
     float* out = X + (size_t)b * MQ_HIDDEN_SIZE;
+    bf16* xw = Xw + (size_t)b * MQ_HIDDEN_SIZE;
 #pragma unroll
     for (int i = 0; i < MQ_HIDDEN_SIZE / 256; ++i) {
-        const int c = (lane + 32 * i) * 8;
-        const uint4 w = *reinterpret_cast<const uint4*>(row + c);
-        *reinterpret_cast<float4*>(out + c) = make_float4(bf16lo(w.x), bf16hi(w.x), bf16lo(w.y), bf16hi(w.y));
-        *reinterpret_cast<float4*>(out + c + 4) = make_float4(bf16lo(w.z), bf16hi(w.z), bf16lo(w.w), bf16hi(w.w));
+        const int c = (lane + 32 * i) * 8;   // lanes 0-15 cover tile 2i, lanes 16-31 tile 2i+1
+        const uint4 e = *reinterpret_cast<const uint4*>(row + c);
+        const uint4 wq = *reinterpret_cast<const uint4*>(w + c);
+        const float v[8] = {bf16lo(e.x), bf16hi(e.x), bf16lo(e.y), bf16hi(e.y),
+                            bf16lo(e.z), bf16hi(e.z), bf16lo(e.w), bf16hi(e.w)};
+        const float wf[8] = {bf16lo(wq.x), bf16hi(wq.x), bf16lo(wq.y), bf16hi(wq.y),
+                             bf16lo(wq.z), bf16hi(wq.z), bf16lo(wq.w), bf16hi(wq.w)};
+        *reinterpret_cast<float4*>(out + c) = make_float4(v[0], v[1], v[2], v[3]);
+        *reinterpret_cast<float4*>(out + c + 4) = make_float4(v[4], v[5], v[6], v[7]);
+        uint32_t pk[4];
+        float sq = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * k] * wf[2 * k], v[2 * k + 1] * wf[2 * k + 1]);
+            pk[k] = *reinterpret_cast<uint32_t*>(&t);
+            sq += v[2 * k] * v[2 * k] + v[2 * k + 1] * v[2 * k + 1];
+        }
+        *reinterpret_cast<uint4*>(xw + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        if ((lane & 15) == 0) ss[b * 8 + 2 * i + (lane >> 4)] = sq;
     }
 }
 
@@ -363,7 +334,7 @@ cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
 }
 
 struct Layout {
-    size_t X, Xn, Qf, part, cnt, attn, act, lastn, best, total;
+    size_t X, Xw, ss, Qf, part, cnt, attn, act, best, total;
 };
 
 int np_of(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : B <= 64 ? 64 : 128; }
@@ -375,13 +346,13 @@ Layout layout(int B, int max_seq) {
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t r = o; o += (bytes + 1023) & ~size_t(1023); return r; };
     L.X = take((size_t)B * 1024 * 4);
-    L.Xn = take(NP * 1024 * 2);
+    L.Xw = take(NP * 1024 * 2);
+    L.ss = take((size_t)B * 8 * 4);
     L.Qf = take((size_t)B * 2048 * 4);
     L.part = take((size_t)B * 8 * C * 2 * PART * 4);
     L.cnt = take((size_t)B * 8 * 4);
     L.attn = take(NP * 2048 * 2);
     L.act = take(NP * 3072 * 2);
-    L.lastn = take(NP * 1024 * 2);
     L.best = take((size_t)B * 8);
     L.total = o;
     return L;
@@ -461,6 +432,9 @@ int launch_small(int total, int kblocks, Small2Args a, const CUtensorMap* tw, co
                     cudaGetLastError();
                     continue;
                 }
+                if (getenv("MQ_SPLIT_VERBOSE"))
+                    fprintf(stderr, "  mode %d NP %d tiles %d: S %d smem %d -> %d clusters\n", MODE, NPV, total, S,
+                            (int)cfg.dynamicSmemBytes, nclusters);
                 if (nclusters >= total || S == 1) {
                     ch.S = S;
                     ch.kpb = kpb;
@@ -543,18 +517,17 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
     if (p->workspace_bytes < L.total) return MQ_ERR_WORKSPACE;
     uint8_t* ws = (uint8_t*)p->workspace;
     float* X = (float*)(ws + L.X);
-    bf16* Xn = (bf16*)(ws + L.Xn);
+    bf16* Xw = (bf16*)(ws + L.Xw);
+    float* ss = (float*)(ws + L.ss);
     float* Qf = (float*)(ws + L.Qf);
     float* part = (float*)(ws + L.part);
     bf16* attn = (bf16*)(ws + L.attn);
     bf16* act = (bf16*)(ws + L.act);
-    bf16* lastn = (bf16*)(ws + L.lastn);
     unsigned long long* best = (unsigned long long*)(ws + L.best);
     const int NP = np_of(B);
     const int C = (p->max_context + ATT_CHUNK - 1) / ATT_CHUNK;
     if (C < 1 || p->max_context > p->max_seq_len) return MQ_ERR_INVALID_ARGUMENT;
     const int norm_blocks = (B + 7) / 8;
-    const float* cX = X;
     cudaError_t e = cudaSuccess;
     auto ok = [&](cudaError_t r) { if (r != cudaSuccess && e == cudaSuccess) e = r; };
     Small2Args ga = {};
@@ -562,15 +535,14 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
     ga.err = p->err_flag;
 
     int* counters = (int*)(ws + L.cnt);
-    ok(launch(embed_step_kernel, dim3(norm_blocks), dim3(256), 0, st, (const int*)p->tokens, (const bf16*)p->embed, X,
-              best, counters, B));
+    ok(launch(embed_step_kernel, dim3(norm_blocks), dim3(256), 0, st, (const int*)p->tokens, (const bf16*)p->embed,
+              (const bf16*)p->layers_host[0].input_layernorm_weight, X, Xw, ss, best, counters, B));
     for (int l = 0; l < p->num_layers; ++l) {
         const LDGLayerWeights& W = p->layers_host[l];
-        ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX, (const bf16*)W.input_layernorm_weight,
-                  Xn, B, norm_blocks, (float4*)nullptr, 0));
         const void* wqkv[3] = {W.q_proj_weight, W.k_proj_weight, W.v_proj_weight};
         const int nqkv[3] = {2048, 1024, 1024};
         Small2Args a = ga;
+        a.ss_in = ss;
         const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * D;
         bf16* kc_l = (bf16*)p->k_cache + layer_off;
         bf16* vc_l = (bf16*)p->v_cache + layer_off;
@@ -584,7 +556,7 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
         a.qkv.v_cache = vc_l;
         a.qkv.seq_stride = p->cache_seq_stride;
         a.qkv.max_seq = p->max_seq_len;
-        int rc = small_gemm<SM_QKV>(wqkv, nqkv, 3, 1024, Xn, NP, a, st);
+        int rc = small_gemm<SM_QKV>(wqkv, nqkv, 3, 1024, Xw, NP, a, st);
         if (rc) return rc;
         ok(launch(attn_unit_kernel, dim3(C, 8, B), dim3(128), 0, st, (const float*)Qf, (const bf16*)kc_l,
                   (const bf16*)vc_l, (const int*)p->positions, p->cache_seq_stride, p->max_seq_len, C,
@@ -594,34 +566,38 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
         a = ga;
         a.out = X;
         a.ldo = 1024;
+        a.w_next = (const bf16*)W.post_attn_layernorm_weight;
+        a.xw_out = Xw;
+        a.ss_out = ss;
         rc = small_gemm<SM_RESID>(wo, no, 1, 2048, attn, NP, a, st);
         if (rc) return rc;
-        ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX,
-                  (const bf16*)W.post_attn_layernorm_weight, Xn, B, norm_blocks, (float4*)nullptr, 0));
         const void* wgu[2] = {W.gate_proj_weight, W.up_proj_weight};
         const int ngu[2] = {3072, 3072};
         a = ga;
         a.act = act;
         a.ldo = 3072;
-        rc = small_gemm<SM_SILU>(wgu, ngu, 2, 1024, Xn, NP, a, st);
+        a.ss_in = ss;
+        rc = small_gemm<SM_SILU>(wgu, ngu, 2, 1024, Xw, NP, a, st);
         if (rc) return rc;
         const void* wd[1] = {W.down_proj_weight};
         const int nd[1] = {1024};
         a = ga;
         a.out = X;
         a.ldo = 1024;
+        a.w_next = (const bf16*)(l + 1 < p->num_layers ? p->layers_host[l + 1].input_layernorm_weight : p->final_norm);
+        a.xw_out = Xw;
+        a.ss_out = ss;
         rc = small_gemm<SM_RESID>(wd, nd, 1, 3072, act, NP, a, st);
         if (rc) return rc;
     }
-    ok(launch(norm_zero_kernel, dim3(norm_blocks), dim3(256), 0, st, cX, (const bf16*)p->final_norm, lastn, B,
-              norm_blocks, (float4*)nullptr, 0));
     const void* wl[1] = {p->lm_head};
     const int nl[1] = {MQ_VOCAB_SIZE};
     Small2Args a = ga;
     a.out = p->logits;
     a.ldo = MQ_VOCAB_SIZE;
     a.best = best;
-    int rc = small_gemm<SM_ARGMAX>(wl, nl, 1, 1024, lastn, NP, a, st);
+    a.ss_in = ss;
+    int rc = small_gemm<SM_ARGMAX>(wl, nl, 1, 1024, Xw, NP, a, st);
     if (rc) return rc;
     ok(launch(finish_step_kernel, dim3((B + 127) / 128), dim3(128), 0, st, (const unsigned long long*)best, p->tokens,
               p->positions, B));

@@ -33,6 +33,7 @@
 #include <cuda_bf16.h>
 
 #include "gemm_tc.cuh"
+#include "megaqwen_b200.h"
 
 namespace mq {
 
@@ -86,6 +87,13 @@ struct Small2Args {
     int* err;
     long long timeout_cycles;
     QkvEpi qkv;              // SM_QKV
+    // RMSNorm folded into the GEMMs: a consumer (SM_QKV, SM_SILU, SM_ARGMAX) scales
+    // row b by 1/rms from ss_in; a producer (SM_RESID) also writes xw_out =
+    // bf16(x * w_next) (the next operand) and ss_out (per-tile sums of squares).
+    const float* ss_in;      // [Bv, 8] or null
+    float* ss_out;           // [Bv, 8]
+    const __nv_bfloat16* w_next;
+    __nv_bfloat16* xw_out;   // [NP, 1024] or null
     unsigned long long* trace;   // optional: 8 %globaltimer stamps per CTA (phase timing)
 };
 
@@ -120,6 +128,107 @@ __device__ __forceinline__ float4 ld_dsmem_f32x4(const float* local, uint32_t ra
 __device__ __forceinline__ uint32_t f32_key(float f) {
     const uint32_t u = __float_as_uint(f);
     return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// 1 / rms of token row b of the residual stream from its per-128-column
+// partial sums of squares (the producer's epilogue wrote them), 1 if absent.
+__device__ __forceinline__ float row_rstd(const float* ss, int b) {
+    if (!ss) return 1.f;
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < MQ_HIDDEN_SIZE / 128; ++i) t += ss[b * (MQ_HIDDEN_SIZE / 128) + i];
+    return rsqrtf(t / (float)MQ_HIDDEN_SIZE + 1e-6f);
+}
+
+// Epilogue operands that do not depend on the split-K sum (fetched early).
+struct EpiPre {
+    float4 x;       // SM_RESID: residual stream value
+    uint2 w;        // SM_RESID: next RMSNorm weight; SM_QKV: q/k norm weight
+    uint2 cs, sn;   // SM_QKV: RoPE cos / sin at the row's position
+    float rs;       // row rstd (SM_QKV, SM_SILU)
+    int p;          // SM_QKV: position
+};
+
+template <int MODE>
+__device__ __forceinline__ EpiPre epi_prefetch(const Small2Args& a, int map, int b, int c4, int n0) {
+    EpiPre e;
+    if (MODE == SM_RESID) {
+        e.x = *reinterpret_cast<const float4*>(a.out + (size_t)b * a.ldo + n0 + c4);
+        if (a.w_next) e.w = *reinterpret_cast<const uint2*>(a.w_next + n0 + c4);
+    }
+    if (MODE == SM_QKV || MODE == SM_SILU) e.rs = row_rstd(a.ss_in, b);
+    if (MODE == SM_QKV) {
+        e.p = a.qkv.pos[b];
+        if (map < 2) {
+            e.w = *reinterpret_cast<const uint2*>((map == 0 ? a.qkv.q_norm : a.qkv.k_norm) + c4);
+            e.cs = *reinterpret_cast<const uint2*>(a.qkv.cos_table + (size_t)e.p * GEMM_BM + c4);
+            e.sn = *reinterpret_cast<const uint2*>(a.qkv.sin_table + (size_t)e.p * GEMM_BM + c4);
+        }
+    }
+    return e;
+}
+
+__device__ __forceinline__ float4 bf16x4(uint2 v) {
+    return make_float4(bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y));
+}
+__device__ __forceinline__ uint2 pack_bf16x4(float a, float b, float c, float d) {
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(a, b), hi = __floats2bfloat162_rn(c, d);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+    return pk;
+}
+
+// The epilogue of one (token row b, columns c4..c4+3) item; one warp holds one
+// full 128-column row of the tile (lane = c4 / 4).
+template <int MODE>
+__device__ __forceinline__ void epi_finish(const Small2Args& a, int map, int tile, int col_off, int n0, int b, int c4,
+                                           float4 acc, float4 acc2, const EpiPre& e) {
+    if (MODE == SM_QKV) {
+        const QkvEpi& q = a.qkv;
+        float4 x = make_float4(acc.x * e.rs, acc.y * e.rs, acc.z * e.rs, acc.w * e.rs);
+        if (map < 2) {
+            const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+            const float rh = rsqrtf(ss / (float)GEMM_BM + 1e-6f);
+            const float4 nw = bf16x4(e.w);
+            x.x *= rh * nw.x; x.y *= rh * nw.y; x.z *= rh * nw.z; x.w *= rh * nw.w;
+            // rotate-half partner dims (c4 +- 64) live in lane ^ 16
+            const float y0 = __shfl_xor_sync(0xffffffffu, x.x, 16), y1 = __shfl_xor_sync(0xffffffffu, x.y, 16);
+            const float y2 = __shfl_xor_sync(0xffffffffu, x.z, 16), y3 = __shfl_xor_sync(0xffffffffu, x.w, 16);
+            const float4 cs = bf16x4(e.cs), sn = bf16x4(e.sn);
+            const float sg = c4 < 64 ? -1.f : 1.f;
+            x.x = x.x * cs.x + sg * y0 * sn.x;
+            x.y = x.y * cs.y + sg * y1 * sn.y;
+            x.z = x.z * cs.z + sg * y2 * sn.z;
+            x.w = x.w * cs.w + sg * y3 * sn.w;
+        }
+        if (map == 0) {
+            *reinterpret_cast<float4*>(q.Qf + (size_t)b * 2048 + n0 + c4) = x;
+        } else {
+            __nv_bfloat16* row = (map == 1 ? q.k_cache : q.v_cache) + b * q.seq_stride +
+                                 ((size_t)tile * q.max_seq + e.p) * GEMM_BM + c4;
+            *reinterpret_cast<uint2*>(row) = pack_bf16x4(x.x, x.y, x.z, x.w);
+        }
+    } else if (MODE == SM_STORE) {
+        *reinterpret_cast<float4*>(a.out + (size_t)b * a.ldo + col_off + n0 + c4) = acc;
+    } else if (MODE == SM_RESID) {
+        float4 x = e.x;
+        x.x += acc.x; x.y += acc.y; x.z += acc.z; x.w += acc.w;
+        *reinterpret_cast<float4*>(a.out + (size_t)b * a.ldo + n0 + c4) = x;
+        if (a.xw_out) {
+            // next GEMM operand bf16(x * w_next) and this tile's sum of squares of the row
+            const float4 w = bf16x4(e.w);
+            *reinterpret_cast<uint2*>(a.xw_out + (size_t)b * MQ_HIDDEN_SIZE + n0 + c4) =
+                pack_bf16x4(x.x * w.x, x.y * w.y, x.z * w.z, x.w * w.w);
+            const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+            if ((threadIdx.x & 31) == 0) a.ss_out[b * (MQ_HIDDEN_SIZE / 128) + n0 / 128] = ss;
+        }
+    } else if (MODE == SM_SILU) {
+        const float g0 = acc.x * e.rs, g1 = acc.y * e.rs, g2 = acc.z * e.rs, g3 = acc.w * e.rs;
+        *reinterpret_cast<uint2*>(a.act + (size_t)b * a.ldo + n0 + c4) =
+            pack_bf16x4(g0 / (1.0f + expf(-g0)) * (acc2.x * e.rs), g1 / (1.0f + expf(-g1)) * (acc2.y * e.rs),
+                        g2 / (1.0f + expf(-g2)) * (acc2.z * e.rs), g3 / (1.0f + expf(-g3)) * (acc2.w * e.rs));
+    }
 }
 
 template <int NP, int MODE>
@@ -273,20 +382,23 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
     }
     tc_fence_before();
     if (MODE == SM_ARGMAX) {
+        __shared__ float s_rstd[NP];
+        for (int b = threadIdx.x; b < args.Bv; b += blockDim.x) s_rstd[b] = row_rstd(args.ss_in, b);
         __syncthreads();
         // logits store (coalesced along n) and per-token tile maximum
         if (warp >= 2) {
             if (args.out) {
                 for (int b = 0; b < args.Bv; ++b)
-                    args.out[(size_t)b * args.ldo + n0 + n] = red[b * Cfg::RED_LD + n];
+                    args.out[(size_t)b * args.ldo + n0 + n] = red[b * Cfg::RED_LD + n] * s_rstd[b];
             }
         }
         for (int b = threadIdx.x; b < args.Bv; b += blockDim.x) {
             const float* row = red + b * Cfg::RED_LD;
-            float bv = row[0];
+            const float rs = s_rstd[b];
+            float bv = row[0] * rs;
             int bi = 0;
             for (int j = 1; j < GEMM_BM; ++j) {
-                const float x = row[j];
+                const float x = row[j] * rs;
                 if (x > bv) { bv = x; bi = j; }
             }
             const unsigned long long key =
@@ -294,17 +406,24 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
             atomicMax(args.best + b, key);
         }
     } else {
-        if (threadIdx.x == 64) trace_stamp(args, 3);
-        cluster_sync_all();
-        if (threadIdx.x == 64) trace_stamp(args, 4);
         // rows (tokens) of this CTA's slice, summed over the cluster's partials in rank order;
-        // thread -> (row, 4 consecutive n); all S peer loads are issued before the sum
+        // thread -> (row, 4 consecutive n), one warp per row.  Operands of the epilogue that do
+        // not depend on the sum are fetched before the cluster barrier.
         const int per = (args.Bv + ksplits - 1) / ksplits;
         const int r = (int)cluster_rank();
         const int b_lo = r * per, b_hi = min(args.Bv, b_lo + per);
-        for (int item = threadIdx.x; item < (b_hi - b_lo) * 32; item += blockDim.x) {
-            const int b = b_lo + (item >> 5), c4 = (item & 31) * 4;
-            float4 acc[Cfg::NW];
+        const int nitems = max(0, b_hi - b_lo) * 32;
+        constexpr int PF = 4;
+        EpiPre pf[PF];
+#pragma unroll
+        for (int k = 0; k < PF; ++k) {
+            const int item = threadIdx.x + k * blockDim.x;
+            if (item < nitems) pf[k] = epi_prefetch<MODE>(args, map, b_lo + (item >> 5), (item & 31) * 4, n0);
+        }
+        if (threadIdx.x == 64) trace_stamp(args, 3);
+        cluster_sync_all();
+        if (threadIdx.x == 64) trace_stamp(args, 4);
+        auto reduce = [&](int b, int c4, float4* acc) {
 #pragma unroll
             for (int a = 0; a < Cfg::NW; ++a) {
                 const float* loc = red + (a * NP + b) * Cfg::RED_LD + c4;
@@ -320,57 +439,23 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmW0, const __grid_constan
                     }
                 acc[a] = sum;
             }
-            if (MODE == SM_QKV) {
-                // one warp = one token row of one head; lane holds dims c4..c4+3
-                const QkvEpi& q = args.qkv;
-                float4 x = acc[0];
-                const int p = q.pos[b];
-                if (map < 2) {
-                    const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
-                    const float rs = rsqrtf(ss / (float)GEMM_BM + 1e-6f);
-                    const __nv_bfloat16* nw = (map == 0 ? q.q_norm : q.k_norm) + c4;
-                    x.x = x.x * rs * __bfloat162float(nw[0]);
-                    x.y = x.y * rs * __bfloat162float(nw[1]);
-                    x.z = x.z * rs * __bfloat162float(nw[2]);
-                    x.w = x.w * rs * __bfloat162float(nw[3]);
-                    // rotate-half partner dims (c4 +- 64) live in lane ^ 16
-                    const float y0 = __shfl_xor_sync(0xffffffffu, x.x, 16), y1 = __shfl_xor_sync(0xffffffffu, x.y, 16);
-                    const float y2 = __shfl_xor_sync(0xffffffffu, x.z, 16), y3 = __shfl_xor_sync(0xffffffffu, x.w, 16);
-                    const __nv_bfloat16* cs = q.cos_table + (size_t)p * GEMM_BM + c4;
-                    const __nv_bfloat16* sn = q.sin_table + (size_t)p * GEMM_BM + c4;
-                    const float sg = c4 < 64 ? -1.f : 1.f;
-                    x.x = x.x * __bfloat162float(cs[0]) + sg * y0 * __bfloat162float(sn[0]);
-                    x.y = x.y * __bfloat162float(cs[1]) + sg * y1 * __bfloat162float(sn[1]);
-                    x.z = x.z * __bfloat162float(cs[2]) + sg * y2 * __bfloat162float(sn[2]);
-                    x.w = x.w * __bfloat162float(cs[3]) + sg * y3 * __bfloat162float(sn[3]);
-                }
-                if (map == 0) {
-                    *reinterpret_cast<float4*>(q.Qf + (size_t)b * 2048 + n0 + c4) = x;
-                } else {
-                    __nv_bfloat16* row = (map == 1 ? q.k_cache : q.v_cache) + b * q.seq_stride +
-                                         ((size_t)tile * q.max_seq + p) * GEMM_BM + c4;
-                    const __nv_bfloat162 lo = __floats2bfloat162_rn(x.x, x.y), hi = __floats2bfloat162_rn(x.z, x.w);
-                    uint2 pk;
-                    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
-                    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
-                    *reinterpret_cast<uint2*>(row) = pk;
-                }
-            } else if (MODE == SM_STORE) {
-                *reinterpret_cast<float4*>(args.out + (size_t)b * args.ldo + col_off + n0 + c4) = acc[0];
-            } else if (MODE == SM_RESID) {
-                float4* o = reinterpret_cast<float4*>(args.out + (size_t)b * args.ldo + n0 + c4);
-                float4 x = *o;
-                x.x += acc[0].x; x.y += acc[0].y; x.z += acc[0].z; x.w += acc[0].w;
-                *o = x;
-            } else {
-                const float4 g = acc[0], u = acc[Cfg::NW - 1];
-                __nv_bfloat162 lo = __floats2bfloat162_rn(g.x / (1.0f + expf(-g.x)) * u.x, g.y / (1.0f + expf(-g.y)) * u.y);
-                __nv_bfloat162 hi = __floats2bfloat162_rn(g.z / (1.0f + expf(-g.z)) * u.z, g.w / (1.0f + expf(-g.w)) * u.w);
-                uint2 pk;
-                pk.x = *reinterpret_cast<uint32_t*>(&lo);
-                pk.y = *reinterpret_cast<uint32_t*>(&hi);
-                *reinterpret_cast<uint2*>(args.act + (size_t)b * args.ldo + n0 + c4) = pk;
+        };
+#pragma unroll
+        for (int k = 0; k < PF; ++k) {
+            const int item = threadIdx.x + k * blockDim.x;
+            if (item < nitems) {
+                const int b = b_lo + (item >> 5), c4 = (item & 31) * 4;
+                float4 acc[Cfg::NW];
+                reduce(b, c4, acc);
+                epi_finish<MODE>(args, map, tile, col_off, n0, b, c4, acc[0], acc[Cfg::NW - 1], pf[k]);
             }
+        }
+        for (int item = threadIdx.x + PF * blockDim.x; item < nitems; item += blockDim.x) {
+            const int b = b_lo + (item >> 5), c4 = (item & 31) * 4;
+            const EpiPre q = epi_prefetch<MODE>(args, map, b, c4, n0);
+            float4 acc[Cfg::NW];
+            reduce(b, c4, acc);
+            epi_finish<MODE>(args, map, tile, col_off, n0, b, c4, acc[0], acc[Cfg::NW - 1], q);
         }
         if (threadIdx.x == 64) trace_stamp(args, 5);
         cluster_sync_all();   // peers read this CTA's partials until here
