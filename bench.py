@@ -220,18 +220,65 @@ def time_device_steps(dec, tok_buf, steps):
     return t_start.elapsed_time(t_end)
 
 
+def run_batch(args, w, cos, sin, dev, hbm, world):
+    """Batched decode (config 5): per batch size and start position, graph-replayed
+    steps over B sequences whose caches are pre-filled with N(0,1) bf16 K/V."""
+    import megaqwen_b200
+    batch = {}
+    g = torch.Generator(device=dev).manual_seed(13)
+    for B in args.batch_sizes:
+        for P in args.batch_positions:
+            MS = P + args.batch_steps + 16
+            bd = megaqwen_b200._C.MegakernelBatchDecoder(w.embed, w.layer_weights_flat(), w.final_norm,
+                                                         w.lm_head, cos, sin, 28, MS, B, True)
+            kc, vc = bd.get_k_cache(), bd.get_v_cache()
+            kc[:, :, :, :P].normal_(generator=g)
+            vc[:, :, :, :P].normal_(generator=g)
+            bd.set_state(torch.arange(B) * 37 + 5, torch.full((B,), P))
+            for _ in range(3):
+                bd.step(False)
+            torch.cuda.synchronize()
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            n = args.batch_steps
+            e0.record()
+            for _ in range(n):
+                bd.step(False)
+            e1.record()
+            torch.cuda.synchronize()
+            bd.check()
+            ms = max_over_ranks(e0.elapsed_time(e1), world) / n
+            pm = P + 3 + n // 2
+            step_bytes = WEIGHT_BYTES + B * KV_BYTES_PER_POS * (pm + 2)
+            batch[f"B{B}_pos{P}"] = {
+                "tok_s": round(world * B / (ms / 1000.0), 1), "tok_s_per_gpu": round(B / (ms / 1000.0), 1),
+                "ms_per_step": round(ms, 4),
+                "roofline_frac": round(step_bytes / (ms / 1000.0) / 1e9 / hbm, 4),
+                "bytes_per_step": step_bytes}
+            del bd, kc, vc
+            torch.cuda.empty_cache()
+    return batch
+
+
 def run_ours(args, rank, world, local):
     import megaqwen_b200
     from megaqwen_b200.weights import make_weights, rope_tables, seeded_prompt
 
     dev = torch.device("cuda", local)
     hbm, hbm_kind = measured_hbm_gbs()
-    max_pos = max(args.sweep + [16 + args.warmup + args.steps]) + 64
+    max_pos = max(args.sweep + [16 + args.warmup + args.steps] +
+                  [p + args.batch_steps + 16 for p in args.batch_positions]) + 64
     w = make_weights(28).to(dev)
     cos, sin = rope_tables(max_pos + 8, device=dev)
     dec = megaqwen_b200.MegakernelDecoder(w.embed, w.layer_weights_flat(), w.final_norm, w.lm_head, cos, sin, 28,
                                           max_pos + 8)
     prompt = seeded_prompt(16).tolist()
+    if args.only_batch:
+        # profiling entry: only the batched-decode measurements, one JSON line
+        batch = run_batch(args, w, cos, sin, dev, hbm, world)
+        if rank == 0:
+            print(json.dumps({"batch_decode": batch}), flush=True)
+        return
 
     # --- headline: config 2, device-fed greedy decode after a 16-token prompt ---
     for t in prompt[:-1]:
@@ -324,40 +371,7 @@ def run_ours(args, rank, world, local):
         sweep_prefill = None
 
     # --- batched decode (config 5): B independent sequences per GPU, one token each per step ---
-    batch = {}
-    if args.batch_sizes:
-        g = torch.Generator(device=dev).manual_seed(13)
-        for B in args.batch_sizes:
-            for P in (16, 1024):
-                MS = P + args.batch_steps + 16
-                bd = megaqwen_b200._C.MegakernelBatchDecoder(w.embed, w.layer_weights_flat(), w.final_norm,
-                                                             w.lm_head, cos, sin, 28, MS, B, True)
-                kc, vc = bd.get_k_cache(), bd.get_v_cache()
-                kc[:, :, :, :P].normal_(generator=g)
-                vc[:, :, :, :P].normal_(generator=g)
-                bd.set_state(torch.arange(B) * 37 + 5, torch.full((B,), P))
-                for _ in range(3):
-                    bd.step(False)
-                torch.cuda.synchronize()
-                barrier(world)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                n = args.batch_steps
-                e0.record()
-                for _ in range(n):
-                    bd.step(False)
-                e1.record()
-                torch.cuda.synchronize()
-                bd.check()
-                ms = max_over_ranks(e0.elapsed_time(e1), world) / n
-                pm = P + 3 + n // 2
-                step_bytes = WEIGHT_BYTES + B * KV_BYTES_PER_POS * (pm + 2)
-                batch[f"B{B}_pos{P}"] = {
-                    "tok_s": round(world * B / (ms / 1000.0), 1), "tok_s_per_gpu": round(B / (ms / 1000.0), 1),
-                    "ms_per_step": round(ms, 4),
-                    "roofline_frac": round(step_bytes / (ms / 1000.0) / 1e9 / hbm, 4),
-                    "bytes_per_step": step_bytes}
-                del bd, kc, vc
-                torch.cuda.empty_cache()
+    batch = run_batch(args, w, cos, sin, dev, hbm, world) if args.batch_sizes else {}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -403,6 +417,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--batch-sizes", type=lambda s: [int(x) for x in s.split(",") if x], default=[16, 64])
     ap.add_argument("--batch-steps", type=int, default=32)
+    ap.add_argument("--batch-positions", type=lambda s: [int(x) for x in s.split(",") if x], default=[16, 1024])
+    ap.add_argument("--only-batch", action="store_true", help="run only the batched-decode measurements")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     args = ap.parse_args()
