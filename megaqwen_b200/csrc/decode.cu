@@ -65,6 +65,7 @@ constexpr int STAGE_BYTES = 32768;
 constexpr int NSTAGES = 6;
 constexpr int MAX_CTAS = 256;
 constexpr int CMAX = MAX_CTAS / NKV;       // max position chunks per kv head
+static_assert(CMAX <= 32, "the split-K combine holds one unit per lane");
 constexpr int PART_STRIDE = 132;           // floats per (unit, head): m, l, pad, pad, acc[128]
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
@@ -81,6 +82,7 @@ static_assert(MV_GROUP * QKV_TILE <= MV_Q * NCW && MV_GROUP * LM_TILE <= MV_Q * 
               MV_GROUP * DOWN_TILE <= MV_Q * NCW, "a group's rows fit MV_Q rows per warp");
 static_assert(MV_GROUP < NSTAGES, "the producer can fill a whole group");
 constexpr int KV_TILE = STAGE_BYTES / (2 * D * 2);   // 64 positions (K and V)
+static_assert(KV_TILE == 64 && 4 * MV_GROUP <= NCW, "attention: 4 groups of 16 positions per tile, one warp each");
 static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <= NCW && LM_TILE <= NCW,
               "one consumer warp per row of a tile");
 
@@ -120,15 +122,15 @@ constexpr int SM_QKVRAW = SM_H + H * 4;                   // fp32 [512]  raw q(2
 constexpr int SM_QN = SM_QKVRAW + 512 * 4;                // fp32 [256]  normed+roped q of 2 heads
 constexpr int SM_KP = SM_QN + 256 * 4;                    // fp32 [128]  bf16-rounded k of position p
 constexpr int SM_VP = SM_KP + 128 * 4;                    // fp32 [128]  bf16-rounded v of position p
-constexpr int SM_ML = SM_VP + 128 * 4;                    // fp32 [16][2][2] per-warp (m, l)
-constexpr int SM_RED = SM_ML + NCW * 4 * 4;               // fp32 [2][16]
+constexpr int SM_ML = SM_VP + 128 * 4;                    // fp32 [16][2][2] per-warp (m, l) + current position
+constexpr int SM_RED = SM_ML + (NCW + 1) * 4 * 4;         // fp32 [2][16]
 constexpr int SM_BEST = SM_RED + 2 * NCW * 4;             // fp32 [16] + int [16]
 constexpr int SM_FLAGS = SM_BEST + 2 * NCW * 4;           // int [4]
 constexpr int SM_BARS = SM_FLAGS + 16;                    // uint64 full[NSTAGES], empty[NSTAGES]
 constexpr int SM_LAYERS = SM_BARS + 2 * NSTAGES * 8;      // LDGLayerWeights [num_layers] copy
 constexpr int SM_SCHED = SM_LAYERS + MQ_MAX_LAYERS * (int)sizeof(LDGLayerWeights);  // Sched
 constexpr int SMEM_BYTES = SM_SCHED + 128;
-static_assert(SM_ACC + NCW * 2 * D * 4 <= SM_H, "attention combine scratch fits in X+H2");
+static_assert(SM_ACC + (NCW + 1) * 2 * D * 4 <= SM_H, "attention combine scratch fits in X+H2");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(SM_BARS % 8 == 0, "mbarrier alignment");
 
@@ -370,12 +372,40 @@ struct Producer {
     }
 };
 
-// Online-softmax state of one attention work unit (two q heads of one kv
-// head); each lane owns head dims 4*lane .. 4*lane+3.
+// Online-softmax state of one warp of an attention work unit (two q heads of
+// one kv head), in mma.sync fragment form.  Scores are in the log2 domain.
+//   S^T = K Q^T on m16n8k16: 16 positions on M, N columns 0/1 = q heads 0/1
+//   rounded to bf16 and columns 2/3 = their bf16 remainders (hi + lo carries
+//   the fp32 q), so one MMA gives near-fp32 scores.  P^T is split the same way
+//   (columns 0/1 = bf16(p), 2/3 = remainder) for O^T = V^T P^T.
+//   Accumulator lane (g, t): t == 0 holds the hi columns of heads 0/1, t == 1
+//   the lo columns; the two are summed at the end of the phase.
+// The B fragments of Q^T live in shared memory (SM_QKVRAW, free once q is
+// normed): uint2 [k-step u*2+half][lane].
 struct AttnState {
-    float q0[4], q1[4], a0[4], a1[4];
-    float m0, l0, m1, l1;
+    float o[4][2][4];       // O^T accumulators per (u, q) block
+    float m[2], l[2];       // running max / sum of the lane's two columns
 };
+
+__device__ __forceinline__ uint32_t movm_t(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+    __nv_bfloat162 t = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&t);
+}
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16(x)); }
+// Head dim held by accumulator row g of block (u, r): lane t loads dims
+// 32u + 8t .. +7 of a row as 16 bytes, register r holds the pair 32u + 8t + 2r.
+__device__ __forceinline__ int attn_vdim(int u, int r, int g) { return 32 * u + 8 * (g >> 1) + 2 * r + (g & 1); }
 
 // Running LM-head argmax of one warp (value, then lowest index on ties).
 struct LmBest {
@@ -746,17 +776,32 @@ struct Consumer {
         if (KIND == 1) {
             AttnState a;
             const float* qn = sm<float>(SM_QN);
+            const int g = lane >> 2, t = lane & 3;
+            const float sc = P.attn_scale * 1.4426950408889634f;   // log2 domain
+            const float* q = qn + (g & 1) * D;                     // column g: head g & 1, hi (g < 2) or lo
+            uint32_t* qbs = sm<uint32_t>(SM_QKVRAW);
+            if (warp == 0) {
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a.q0[i] = qn[4 * lane + i] * P.attn_scale;
-                a.q1[i] = qn[D + 4 * lane + i] * P.attn_scale;
-                a.a0[i] = 0.f;
-                a.a1[i] = 0.f;
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf)
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const int d0 = 32 * u + 8 * t + 4 * hf + 2 * j;
+                        const float x0 = q[d0] * sc, x1 = q[d0 + 1] * sc;
+                        const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+                        qbs[(u * 2 + hf) * 64 + lane * 2 + j] =
+                            g < 2 ? pack2_bf16(h0, h1) : g < 4 ? pack2_bf16(x0 - h0, x1 - h1) : 0u;
+                    }
             }
-            a.m0 = a.m1 = -INFINITY;
-            a.l0 = a.l1 = 0.f;
-            for_tiles(P, S, PH_ATTN, l,
-                      [&](int r, int nr, const char*, int b1, const char*, int) { tile<1>(PH_ATTN, l, r, nr, b1, &a, nullptr); });
+            named_bar_sync(BAR_CONSUMERS, NCT);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) a.o[u][qq][0] = a.o[u][qq][1] = a.o[u][qq][2] = a.o[u][qq][3] = 0.f;
+            a.m[0] = a.m[1] = -INFINITY;
+            a.l[0] = a.l[1] = 0.f;
+            attn_phase(a, l);
             end_attn(a, l);
             return true;
         }
@@ -884,48 +929,103 @@ struct Consumer {
         }
     }
 
-    __device__ __forceinline__ void attn_pos(AttnState& a, const uint2 kq, const uint2 vq) {
-        float k0 = bf16lo(kq.x), k1 = bf16hi(kq.x), k2 = bf16lo(kq.y), k3 = bf16hi(kq.y);
-        float s0 = a.q0[0] * k0 + a.q0[1] * k1 + a.q0[2] * k2 + a.q0[3] * k3;
-        float s1 = a.q1[0] * k0 + a.q1[1] * k1 + a.q1[2] * k2 + a.q1[3] * k3;
+    // 16 cached positions (rows 16 grp .. +15 of a staged K/V tile, n valid) into
+    // this warp's attention state.  K rows are the A fragments of S^T as
+    // loaded (16 bytes per lane; the head-dim order is permuted identically in
+    // Q), V^T and P^T come from movmatrix transposes.
+    __device__ __forceinline__ void attn_group(AttnState& a, const uint8_t* kb, const uint8_t* vb, int grp, int n) {
+        const int g = lane >> 2, t = lane & 3;
+        const int ra = 16 * grp + g, rb = ra + 8;
+        const bool va = ra < n, vbk = rb < n;
+        const uint2* qbs = sm<uint2>(SM_QKVRAW);
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+        for (int u = 0; u < 4; ++u) {
+            const uint4 k0 = va ? *reinterpret_cast<const uint4*>(kb + ra * (D * 2) + 64 * u + 16 * t) : make_uint4(0, 0, 0, 0);
+            const uint4 k1 = vbk ? *reinterpret_cast<const uint4*>(kb + rb * (D * 2) + 64 * u + 16 * t) : make_uint4(0, 0, 0, 0);
+            const uint32_t a0[4] = {k0.x, k1.x, k0.y, k1.y};
+            const uint32_t a1[4] = {k0.z, k1.z, k0.w, k1.w};
+            const uint2 q0 = qbs[(u * 2 + 0) * 32 + lane], q1 = qbs[(u * 2 + 1) * 32 + lane];
+            mma16816(sc, a0, q0.x, q0.y);
+            mma16816(sc, a1, q1.x, q1.y);
         }
-        float v0 = bf16lo(vq.x), v1 = bf16hi(vq.x), v2 = bf16lo(vq.y), v3 = bf16hi(vq.y);
-        float n0 = fmaxf(a.m0, s0), c0 = expf(a.m0 - n0), p0 = expf(s0 - n0);
-        float n1 = fmaxf(a.m1, s1), c1 = expf(a.m1 - n1), p1 = expf(s1 - n1);
-        a.l0 = a.l0 * c0 + p0;
-        a.l1 = a.l1 * c1 + p1;
-        a.a0[0] = a.a0[0] * c0 + p0 * v0; a.a0[1] = a.a0[1] * c0 + p0 * v1; a.a0[2] = a.a0[2] * c0 + p0 * v2; a.a0[3] = a.a0[3] * c0 + p0 * v3;
-        a.a1[0] = a.a1[0] * c1 + p1 * v0; a.a1[1] = a.a1[1] * c1 + p1 * v1; a.a1[2] = a.a1[2] * c1 + p1 * v2; a.a1[3] = a.a1[3] * c1 + p1 * v3;
-        a.m0 = n0;
-        a.m1 = n1;
-    }
-
-    template <int KIND>
-    __device__ __forceinline__ void tile(int phase, int l, int r0, int nrows, int b1, AttnState* a, LmBest* bst) {
-        const uint32_t s = n % NSTAGES, par = (n / NSTAGES) & 1u;
-        const bool tr = P.trace && ct == 0 && n < 320;
-        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 513 + 4 * n] = globaltimer_ns();
-        ++n;
-        const bool got = wait_full(s, par, phase, l);
-        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 514 + 4 * (n - 1)] = globaltimer_ns();
-        const uint8_t* st = g_smem + SM_STAGES + s * STAGE_BYTES;
-        if (KIND == 1) {
-            if (got) {
-                const uint8_t* kb = st;
-                const uint8_t* vb = st + b1;
-                for (int t = warp; t < nrows; t += NCW) {
-                    uint2 kq = *reinterpret_cast<const uint2*>(kb + t * D * 2 + lane * 8);
-                    uint2 vq = *reinterpret_cast<const uint2*>(vb + t * D * 2 + lane * 8);
-                    attn_pos(*a, kq, vq);
-                }
-                release(s);
+        // hi + lo columns: lanes t = 0 and t = 1 both get the full scores of heads 0/1
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[i] += __shfl_xor_sync(0xffffffffu, sc[i], 1);
+        if (!va) sc[0] = sc[1] = -INFINITY;
+        if (!vbk) sc[2] = sc[3] = -INFINITY;
+        float mx[2] = {fmaxf(sc[0], sc[2]), fmaxf(sc[1], sc[3])};
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+            mx[0] = fmaxf(mx[0], __shfl_xor_sync(0xffffffffu, mx[0], o));
+            mx[1] = fmaxf(mx[1], __shfl_xor_sync(0xffffffffu, mx[1], o));
+        }
+        float corr[2];
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+            const float mn = fmaxf(a.m[r], mx[r]);
+            corr[r] = exp2f(a.m[r] - mn);
+            a.m[r] = mn;
+            a.l[r] *= corr[r];
+        }
+        const float e0 = exp2f(sc[0] - a.m[0]), e1 = exp2f(sc[1] - a.m[1]);
+        const float e2 = exp2f(sc[2] - a.m[0]), e3 = exp2f(sc[3] - a.m[1]);
+        a.l[0] += e0 + e2;
+        a.l[1] += e1 + e3;
+        // P^T columns: t == 0 -> bf16(p), t == 1 -> remainder, t >= 2 -> 0
+        uint32_t pa, pb;
+        if (t == 0) {
+            pa = pack2_bf16(e0, e1);
+            pb = pack2_bf16(e2, e3);
+        } else if (t == 1) {
+            pa = pack2_bf16(e0 - bf16_round(e0), e1 - bf16_round(e1));
+            pb = pack2_bf16(e2 - bf16_round(e2), e3 - bf16_round(e3));
+        } else {
+            pa = pb = 0u;
+        }
+        const uint32_t pb0 = movm_t(pa), pb1 = movm_t(pb);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint4 v0 = va ? *reinterpret_cast<const uint4*>(vb + ra * (D * 2) + 64 * u + 16 * t) : make_uint4(0, 0, 0, 0);
+            const uint4 v1 = vbk ? *reinterpret_cast<const uint4*>(vb + rb * (D * 2) + 64 * u + 16 * t) : make_uint4(0, 0, 0, 0);
+            const uint32_t r0[4] = {v0.x, v0.y, v0.z, v0.w};
+            const uint32_t r1[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) {
+                float* o = a.o[u][qq];
+                o[0] *= corr[0]; o[1] *= corr[1]; o[2] *= corr[0]; o[3] *= corr[1];
+                const uint32_t av[4] = {movm_t(r0[qq]), movm_t(r0[qq + 2]), movm_t(r1[qq]), movm_t(r1[qq + 2])};
+                mma16816(o, av, pb0, pb1);
             }
         }
-        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 515 + 4 * (n - 1)] = globaltimer_ns();
+    }
+
+    // The attention unit's cached positions: K/V tiles of KV_TILE positions (the
+    // tiling of for_tiles), consumed MV_GROUP stages at a time so that 12 of
+    // the 15 warps work at once: warp w takes 16-position group w % 4 of tile
+    // w / 4 of the batch.
+    __device__ __forceinline__ void attn_phase(AttnState& a, int l) {
+        const int ntiles = (S.kv_e - S.kv_s + KV_TILE - 1) / KV_TILE;
+        for (int g0 = 0; g0 < ntiles; g0 += MV_GROUP) {
+            const int g1 = min(ntiles, g0 + MV_GROUP);
+            bool got = true;
+            for (int i = g0; i < g1; ++i) {
+                const uint32_t t = n + (uint32_t)(i - g0);
+                got = wait_full(t % NSTAGES, (t / NSTAGES) & 1u, PH_ATTN, l) && got;
+            }
+            if (got) {
+                const int ti = g0 + (warp >> 2), grp = warp & 3;
+                if (ti < g1) {
+                    const int nrows = min(S.kv_e - (S.kv_s + ti * KV_TILE), KV_TILE);
+                    if (grp * 16 < nrows) {
+                        const uint8_t* st = g_smem + SM_STAGES + ((n + (uint32_t)(ti - g0)) % NSTAGES) * STAGE_BYTES;
+                        attn_group(a, st, st + nrows * D * 2, grp, nrows);
+                    }
+                }
+                for (int i = g0; i < g1; ++i) release((n + (uint32_t)(i - g0)) % NSTAGES);
+            }
+            n += (uint32_t)(g1 - g0);
+        }
     }
 
     __device__ __forceinline__ void release(uint32_t s) {
@@ -939,44 +1039,69 @@ struct Consumer {
     __device__ __forceinline__ void end_attn(AttnState& a, int l) {
         float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);   // [16][2][128]
         float* ml = reinterpret_cast<float*>(g_smem + SM_ML);     // [16][2][2]
-        if (ok && S.last && warp == NCW - 1) {
-            // the current position (on the warp with the fewest cached positions),
-            // from the bf16-rounded values in shared memory
-            const float* kp = reinterpret_cast<const float*>(g_smem + SM_KP);
-            const float* vp = reinterpret_cast<const float*>(g_smem + SM_VP);
-            float k0 = kp[4 * lane], k1 = kp[4 * lane + 1], k2 = kp[4 * lane + 2], k3 = kp[4 * lane + 3];
-            float s0 = a.q0[0] * k0 + a.q0[1] * k1 + a.q0[2] * k2 + a.q0[3] * k3;
-            float s1 = a.q1[0] * k0 + a.q1[1] * k1 + a.q1[2] * k2 + a.q1[3] * k3;
-            s0 = warp_sum(s0);
-            s1 = warp_sum(s1);
-            float n0 = fmaxf(a.m0, s0), c0 = expf(a.m0 - n0), p0 = expf(s0 - n0);
-            float n1 = fmaxf(a.m1, s1), c1 = expf(a.m1 - n1), p1 = expf(s1 - n1);
-            a.l0 = a.l0 * c0 + p0;
-            a.l1 = a.l1 * c1 + p1;
+        const int g = lane >> 2, t = lane & 3;
+        // this warp: row-group sums, then hi + lo accumulator columns
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float vv = vp[4 * lane + i];
-                a.a0[i] = a.a0[i] * c0 + p0 * vv;
-                a.a1[i] = a.a1[i] * c1 + p1 * vv;
-            }
-            a.m0 = n0;
-            a.m1 = n1;
+        for (int o = 4; o < 32; o <<= 1) {
+            a.l[0] += __shfl_xor_sync(0xffffffffu, a.l[0], o);
+            a.l[1] += __shfl_xor_sync(0xffffffffu, a.l[1], o);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) a.o[u][qq][i] += __shfl_xor_sync(0xffffffffu, a.o[u][qq][i], 1);
+        if (t == 0) {
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+#pragma unroll
+                for (int qq = 0; qq < 2; ++qq) {
+                    const int d0 = attn_vdim(u, qq, g), d1 = attn_vdim(u, qq + 2, g);
+                    acc[(warp * 2 + 0) * D + d0] = a.o[u][qq][0];
+                    acc[(warp * 2 + 1) * D + d0] = a.o[u][qq][1];
+                    acc[(warp * 2 + 0) * D + d1] = a.o[u][qq][2];
+                    acc[(warp * 2 + 1) * D + d1] = a.o[u][qq][3];
+                }
         }
         if (lane == 0) {
-            ml[warp * 4 + 0] = a.m0; ml[warp * 4 + 1] = a.l0;
-            ml[warp * 4 + 2] = a.m1; ml[warp * 4 + 3] = a.l1;
+            ml[warp * 4 + 0] = a.m[0]; ml[warp * 4 + 1] = a.l[0];
+            ml[warp * 4 + 2] = a.m[1]; ml[warp * 4 + 3] = a.l[1];
         }
-        *reinterpret_cast<float4*>(acc + (warp * 2 + 0) * D + 4 * lane) = make_float4(a.a0[0], a.a0[1], a.a0[2], a.a0[3]);
-        *reinterpret_cast<float4*>(acc + (warp * 2 + 1) * D + 4 * lane) = make_float4(a.a1[0], a.a1[1], a.a1[2], a.a1[3]);
+        if (warp == NCW - 1) {
+            // entry NCW: the current position (last unit only), fp32 q.k of the
+            // bf16-rounded k/v held in shared memory
+            const bool cur = ok && S.last;
+            const float* qn = sm<float>(SM_QN);
+            const float* kp = reinterpret_cast<const float*>(g_smem + SM_KP);
+            const float* vp = reinterpret_cast<const float*>(g_smem + SM_VP);
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                s0 += qn[4 * lane + i] * kp[4 * lane + i];
+                s1 += qn[D + 4 * lane + i] * kp[4 * lane + i];
+            }
+            s0 = warp_sum(s0) * (P.attn_scale * 1.4426950408889634f);
+            s1 = warp_sum(s1) * (P.attn_scale * 1.4426950408889634f);
+            if (lane == 0) {
+                ml[NCW * 4 + 0] = cur ? s0 : -INFINITY; ml[NCW * 4 + 1] = cur ? 1.f : 0.f;
+                ml[NCW * 4 + 2] = cur ? s1 : -INFINITY; ml[NCW * 4 + 3] = cur ? 1.f : 0.f;
+            }
+            const float4 v4 = cur ? *reinterpret_cast<const float4*>(vp + 4 * lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(acc + (NCW * 2 + 0) * D + 4 * lane) = v4;
+            *reinterpret_cast<float4*>(acc + (NCW * 2 + 1) * D + 4 * lane) = v4;
+        }
         named_bar_sync(BAR_CONSUMERS, NCT);
         float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
         const int h = warp;  // warps 0 and 1 combine heads 0 and 1
         if (warp < 2) {
 #pragma unroll
-            for (int w = 0; w < NCW; ++w) M = fmaxf(M, ml[w * 4 + 2 * h]);
+            for (int w = 0; w <= NCW; ++w) M = fmaxf(M, ml[w * 4 + 2 * h]);
 #pragma unroll
-            for (int w = 0; w < NCW; ++w) {
-                float e = expf(ml[w * 4 + 2 * h] - M);
+            for (int w = 0; w <= NCW; ++w) {
+                const float mw = ml[w * 4 + 2 * h];
+                if (mw == -INFINITY) continue;   // no positions in this entry
+                float e = exp2f(mw - M);
                 Ls += ml[w * 4 + 2 * h + 1] * e;
                 float4 a = *reinterpret_cast<const float4*>(acc + (w * 2 + h) * D + 4 * lane);
                 A[0] += a.x * e; A[1] += a.y * e; A[2] += a.z * e; A[3] += a.w * e;
@@ -1013,14 +1138,24 @@ struct Consumer {
         }
         named_bar_sync(BAR_CONSUMERS, NCT);
         if (f[2] && warp < 2 && ok) {
-            float gm = -INFINITY;
-            for (int j = 0; j < S.C; ++j) gm = fmaxf(gm, ld_relaxed_f32(part_of(P, S.ug, j, h)));
-            float gl = 0.f, G4[4] = {0.f, 0.f, 0.f, 0.f};
+            // all units' (max, sum) in parallel (lane j holds unit j), then the
+            // accumulators with independent loads
+            float mj = -INFINITY, lj = 0.f;
+            if (lane < S.C) {
+                const float* pp = part_of(P, S.ug, lane, h);
+                mj = __ldcg(pp);
+                lj = __ldcg(pp + 1);
+            }
+            float gm = mj;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+            const float ej = lane < S.C ? exp2f(mj - gm) : 0.f;   // unit maxima are in the log2 domain
+            const float gl = warp_sum(lj * ej);
+            float G4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 6
             for (int j = 0; j < S.C; ++j) {
-                const float* pp = part_of(P, S.ug, j, h);
-                float e = expf(ld_relaxed_f32(pp) - gm);
-                gl += ld_relaxed_f32(pp + 1) * e;
-                float4 a = __ldcg(reinterpret_cast<const float4*>(pp + 4 + 4 * lane));
+                const float e = __shfl_sync(0xffffffffu, ej, j);
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(part_of(P, S.ug, j, h) + 4 + 4 * lane));
                 G4[0] += a.x * e; G4[1] += a.y * e; G4[2] += a.z * e; G4[3] += a.w * e;
             }
             float inv = 1.0f / gl;
