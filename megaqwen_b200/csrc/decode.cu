@@ -776,24 +776,20 @@ struct Consumer {
         if (KIND == 1) {
             AttnState a;
             const float* qn = sm<float>(SM_QN);
-            const int g = lane >> 2, t = lane & 3;
             const float sc = P.attn_scale * 1.4426950408889634f;   // log2 domain
-            const float* q = qn + (g & 1) * D;                     // column g: head g & 1, hi (g < 2) or lo
             uint32_t* qbs = sm<uint32_t>(SM_QKVRAW);
-            if (warp == 0) {
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf)
-#pragma unroll
-                    for (int j = 0; j < 2; ++j) {
-                        const int d0 = 32 * u + 8 * t + 4 * hf + 2 * j;
-                        const float x0 = q[d0] * sc, x1 = q[d0 + 1] * sc;
-                        const float h0 = bf16_round(x0), h1 = bf16_round(x1);
-                        qbs[(u * 2 + hf) * 64 + lane * 2 + j] =
-                            g < 2 ? pack2_bf16(h0, h1) : g < 4 ? pack2_bf16(x0 - h0, x1 - h1) : 0u;
-                    }
+            // word w = (k-step * 32 + lane') * 2 + j of the B fragments, one or two per thread;
+            // column g' = lane' / 4: head g' & 1, hi (g' < 2) or remainder (g' < 4), else 0
+            for (int w = ct; w < 512; w += NCT) {
+                const int jj = w & 1, lw = (w >> 1) & 31, ks = w >> 6;
+                const int gw = lw >> 2, tw = lw & 3;
+                const int d0 = 32 * (ks >> 1) + 8 * tw + 4 * (ks & 1) + 2 * jj;
+                const float* q = qn + (gw & 1) * D;
+                const float x0 = q[d0] * sc, x1 = q[d0 + 1] * sc;
+                const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+                qbs[w] = gw < 2 ? pack2_bf16(h0, h1) : gw < 4 ? pack2_bf16(x0 - h0, x1 - h1) : 0u;
             }
+            attn_stamp(l, 0);
             named_bar_sync(BAR_CONSUMERS, NCT);
 #pragma unroll
             for (int u = 0; u < 4; ++u)
@@ -801,8 +797,11 @@ struct Consumer {
                 for (int qq = 0; qq < 2; ++qq) a.o[u][qq][0] = a.o[u][qq][1] = a.o[u][qq][2] = a.o[u][qq][3] = 0.f;
             a.m[0] = a.m[1] = -INFINITY;
             a.l[0] = a.l[1] = 0.f;
+            attn_stamp(l, 1);
             attn_phase(a, l);
+            attn_stamp(l, 2);
             end_attn(a, l);
+            attn_stamp(l, 4);
             return true;
         }
         float xr[32];  // K=1024 phases: this lane's input chunks lane + 32u, read once per phase
@@ -1036,6 +1035,18 @@ struct Consumer {
         }
     }
 
+    // Trace slots 340 + 5 l + k of the attention phase (k: 0 q fragments built,
+    // 1 start of tiles, 2 tiles done, 3 local merge done, 4 phase done),
+    // consumer thread 0.
+    __device__ __forceinline__ void attn_stamp(int l, int k) {
+        if (P.trace && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 340 + 5 * l + k] = globaltimer_ns();
+    }
+    // extra split-K combine stamps (layer 14 only): slots 480 + k
+    __device__ __forceinline__ void comb_stamp(int l, int k) {
+        if (P.trace && l == 14 && (threadIdx.x & 31) == 0 && warp == 0)
+            P.trace[(size_t)S.c * TRACE_STRIDE + 480 + k] = globaltimer_ns();
+    }
+
     __device__ __forceinline__ void end_attn(AttnState& a, int l) {
         float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);   // [16][2][128]
         float* ml = reinterpret_cast<float*>(g_smem + SM_ML);     // [16][2][2]
@@ -1095,16 +1106,18 @@ struct Consumer {
         float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
         const int h = warp;  // warps 0 and 1 combine heads 0 and 1
         if (warp < 2) {
+            // lane w <= NCW holds entry w's (max, sum); the weights are shuffled to all lanes
+            const float mw = lane <= NCW ? ml[lane * 4 + 2 * h] : -INFINITY;
+            M = mw;
 #pragma unroll
-            for (int w = 0; w <= NCW; ++w) M = fmaxf(M, ml[w * 4 + 2 * h]);
+            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+            const float ew = mw == -INFINITY ? 0.f : exp2f(mw - M);   // entries without positions weigh 0
+            Ls = warp_sum(lane <= NCW ? ml[lane * 4 + 2 * h + 1] * ew : 0.f);
 #pragma unroll
             for (int w = 0; w <= NCW; ++w) {
-                const float mw = ml[w * 4 + 2 * h];
-                if (mw == -INFINITY) continue;   // no positions in this entry
-                float e = exp2f(mw - M);
-                Ls += ml[w * 4 + 2 * h + 1] * e;
-                float4 a = *reinterpret_cast<const float4*>(acc + (w * 2 + h) * D + 4 * lane);
-                A[0] += a.x * e; A[1] += a.y * e; A[2] += a.z * e; A[3] += a.w * e;
+                const float e = __shfl_sync(0xffffffffu, ew, w);
+                const float4 av = *reinterpret_cast<const float4*>(acc + (w * 2 + h) * D + 4 * lane);
+                A[0] += av.x * e; A[1] += av.y * e; A[2] += av.z * e; A[3] += av.w * e;
             }
         }
         const uint32_t tag = tag_of(S, l);
@@ -1118,49 +1131,77 @@ struct Consumer {
             return;
         }
         // split-K: publish the partial, the last unit of this kv head combines
+        attn_stamp(l, 3);
         volatile int* f = flags();
         if (warp < 2) {
             float* pp = part_of(P, S.ug, S.uj, h);
             if (lane == 0) { pp[0] = M; pp[1] = Ls; }
             *reinterpret_cast<float4*>(pp + 4 + 4 * lane) = make_float4(A[0], A[1], A[2], A[3]);
-            __threadfence();
         }
         named_bar_sync(BAR_CONSUMERS, NCT);
         if (ct == 0) {
+            // release (cumulative over the CTA's partial stores ordered by the barrier) and acquire
             Control* C = ctrl_of(P);
-            uint32_t old = atomicAdd(&C->attn_count[S.ug], 1u);
-            int last = (old == (uint32_t)(S.C - 1));
-            if (last) {
-                atomicExch(&C->attn_count[S.ug], 0u);
-                __threadfence();
-            }
+            uint32_t old;
+            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&C->attn_count[S.ug]) : "memory");
+            const int last = (old == (uint32_t)(S.C - 1));
+            if (last) atomicExch(&C->attn_count[S.ug], 0u);
             f[2] = last;
         }
+        comb_stamp(l, 0);
         named_bar_sync(BAR_CONSUMERS, NCT);
-        if (f[2] && warp < 2 && ok) {
-            // all units' (max, sum) in parallel (lane j holds unit j), then the
-            // accumulators with independent loads
-            float mj = -INFINITY, lj = 0.f;
+        comb_stamp(l, 1);
+        if (!f[2]) return;   // the flag is CTA-uniform: every consumer thread takes the same path
+        // combine the S.C partials of both heads: warp w sums units w, w + NCW, .. into
+        // shared memory (one L2 round trip for all units), warps 0/1 add the NCW sums
+        float* cs = reinterpret_cast<float*>(g_smem + SM_ACC);   // [NCW][2][128]
+        {
+            float mj[2] = {-INFINITY, -INFINITY}, lj[2] = {0.f, 0.f};
             if (lane < S.C) {
-                const float* pp = part_of(P, S.ug, lane, h);
-                mj = __ldcg(pp);
-                lj = __ldcg(pp + 1);
-            }
-            float gm = mj;
 #pragma unroll
-            for (int o = 16; o > 0; o >>= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-            const float ej = lane < S.C ? exp2f(mj - gm) : 0.f;   // unit maxima are in the log2 domain
-            const float gl = warp_sum(lj * ej);
-            float G4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 6
-            for (int j = 0; j < S.C; ++j) {
-                const float e = __shfl_sync(0xffffffffu, ej, j);
-                const float4 a = __ldcg(reinterpret_cast<const float4*>(part_of(P, S.ug, j, h) + 4 + 4 * lane));
-                G4[0] += a.x * e; G4[1] += a.y * e; G4[2] += a.z * e; G4[3] += a.w * e;
+                for (int hh = 0; hh < 2; ++hh) {
+                    const float* pp = part_of(P, S.ug, lane, hh);
+                    mj[hh] = __ldcg(pp);
+                    lj[hh] = __ldcg(pp + 1);
+                }
             }
-            float inv = 1.0f / gl;
+            float gm[2], ej[2], gl[2];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(G4[i] * inv, tag));
+            for (int hh = 0; hh < 2; ++hh) {
+                gm[hh] = mj[hh];
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) gm[hh] = fmaxf(gm[hh], __shfl_xor_sync(0xffffffffu, gm[hh], o));
+                ej[hh] = lane < S.C ? exp2f(mj[hh] - gm[hh]) : 0.f;   // unit maxima are in the log2 domain
+                gl[hh] = warp_sum(lj[hh] * ej[hh]);
+            }
+            float4 g4[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+            for (int j2 = warp; j2 < S.C; j2 += NCW) {
+#pragma unroll
+                for (int hh = 0; hh < 2; ++hh) {
+                    const float e = __shfl_sync(0xffffffffu, ej[hh], j2);
+                    const float4 av = __ldcg(reinterpret_cast<const float4*>(part_of(P, S.ug, j2, hh) + 4 + 4 * lane));
+                    g4[hh].x += av.x * e; g4[hh].y += av.y * e; g4[hh].z += av.z * e; g4[hh].w += av.w * e;
+                }
+            }
+            comb_stamp(l, 2);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) *reinterpret_cast<float4*>(cs + (warp * 2 + hh) * D + 4 * lane) = g4[hh];
+            named_bar_sync(BAR_CONSUMERS, NCT);
+            if (warp < 2) {
+                float G4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int w = 0; w < NCW; ++w) {
+                    const float4 av = *reinterpret_cast<const float4*>(cs + (w * 2 + h) * D + 4 * lane);
+                    G4[0] += av.x; G4[1] += av.y; G4[2] += av.z; G4[3] += av.w;
+                }
+                comb_stamp(l, 3);
+                const float inv = 1.0f / gl[h];
+                if (ok) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(G4[i] * inv, tag));
+                }
+                comb_stamp(l, 4);
+            }
         }
     }
 
