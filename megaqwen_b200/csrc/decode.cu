@@ -62,7 +62,7 @@ constexpr int NCW = 15;                    // consumer warps (16 warps in all: 1
 constexpr int NCT = NCW * 32;              // consumer threads
 constexpr int NTHREADS = NCT + 32;         // + one producer warp
 constexpr int STAGE_BYTES = 32768;
-constexpr int NSTAGES = 6;
+constexpr int NSTAGES = 5;
 constexpr int MAX_CTAS = 256;
 constexpr int CMAX = MAX_CTAS / NKV;       // max position chunks per kv head
 static_assert(CMAX <= 32, "the split-K combine holds one unit per lane");
@@ -854,11 +854,14 @@ struct Consumer {
         const uint32_t tag = tag_of(S, l);
         for (int g0 = 0; g0 < ntiles; g0 += MV_GROUP) {
             const int g1 = min(ntiles, g0 + MV_GROUP);
+            const bool tr = P.trace && ct == 0 && n < 320;
+            if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 513 + 4 * n] = globaltimer_ns();
             bool got = true;
             for (int i = g0; i < g1; ++i) {
                 const uint32_t t = n + (uint32_t)(i - g0);
                 got = wait_full(t % NSTAGES, (t / NSTAGES) & 1u, phase, l) && got;
             }
+            if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 514 + 4 * n] = globaltimer_ns();
             const int j0 = g0 * T, j1 = min(g1 * T, R);
             if (got) {
                 float acc[MV_Q], up[MV_Q];
@@ -922,6 +925,7 @@ struct Consumer {
                         }
                     }
                 }
+                if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 515 + 4 * n] = globaltimer_ns();
                 for (int i = g0; i < g1; ++i) release((n + (uint32_t)(i - g0)) % NSTAGES);
             }
             n += (uint32_t)(g1 - g0);
