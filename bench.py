@@ -412,7 +412,7 @@ def main():
     ap.add_argument("--steps", type=int, default=512)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 128, 512, 2048, 8192])
+    ap.add_argument("--sweep", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 128, 512, 2048, 8192, 32768])
     ap.add_argument("--sweep-steps", type=int, default=64)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--batch-sizes", type=lambda s: [int(x) for x in s.split(",") if x], default=[16, 64])

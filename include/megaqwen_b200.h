@@ -14,6 +14,7 @@
  *   launch_ldg_decode             csrc/megakernel/fused_decode_ldg.cu:893-969
  *   launch_ldg_decode_with_logits csrc/megakernel/fused_decode_ldg.cu:972-1057
  *   launch_prefill_float          csrc/megakernel/fused_prefill.cu:601-867
+ *   launch_prefill_megakernel     csrc/megakernel/fused_prefill_megakernel.cu:938-1020
  */
 #ifndef MEGAQWEN_B200_H
 #define MEGAQWEN_B200_H
@@ -229,6 +230,19 @@ void launch_prefill_float(const int* input_token_ids, int* output_token_id, int 
                           void* gate_out, void* up_out, void* mlp_intermediate, void* down_out, void* final_hidden,
                           void* block_max_vals, void* block_max_idxs, void* hidden_bf16_out, int num_layers,
                           int max_seq_len, float attn_scale, void* cublas_handle, cudaStream_t stream);
+/* launch_prefill_megakernel: the reference's short-prompt prefill launcher,
+ * same arguments (fused_prefill_megakernel.cu:938-966).  layer_weights is a
+ * DEVICE array there (megakernel_decode.py:911-916); it is read back to the
+ * host and the prompt runs through the tensor-core prefill.  The fp32 scratch
+ * buffers are accepted and not used.  Status: mq_prefill_get_last_error(). */
+void launch_prefill_megakernel(const int* token_ids, int* output_token_id, int seq_len, const void* embed_weight,
+                               const PrefillLayerWeights* layer_weights, const void* final_norm_weight,
+                               const void* lm_head_weight, const void* cos_table, const void* sin_table,
+                               void* k_cache, void* v_cache, void* hidden, void* residual, void* normalized,
+                               void* q_proj, void* k_proj, void* v_proj, void* attn_out, void* mlp_intermediate,
+                               void* final_hidden, void* hidden_bf16_out, void* block_max_vals,
+                               void* block_max_idxs, int num_layers, int max_seq_len, float attn_scale,
+                               cudaStream_t stream);
 int mq_prefill_get_last_error(void);
 
 /* ---- batched decode -----------------------------------------------------------

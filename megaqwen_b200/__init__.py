@@ -21,6 +21,7 @@ except ImportError as exc:  # pragma: no cover - exercised only on broken instal
 MegakernelDecoder = _C.MegakernelDecoder
 MegakernelPrefillDecoder = _C.MegakernelPrefillDecoder
 MegakernelFusedPrefillDecoder = _C.MegakernelFusedPrefillDecoder
+MegakernelBatchDecoder = _C.MegakernelBatchDecoder
 init_ldg_layer_weights = _C.init_ldg_layer_weights
 init_ldg_embed_weight = _C.init_ldg_embed_weight
 decode_ldg = _C.decode_ldg
@@ -30,6 +31,7 @@ __all__ = [
     "MegakernelDecoder",
     "MegakernelPrefillDecoder",
     "MegakernelFusedPrefillDecoder",
+    "MegakernelBatchDecoder",
     "init_ldg_layer_weights",
     "init_ldg_embed_weight",
     "decode_ldg",

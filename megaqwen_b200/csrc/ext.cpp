@@ -720,6 +720,16 @@ public:
         return tokens_;
     }
 
+    // The additive batch entrypoint: consumes tokens[b] (int [batch]) at each
+    // sequence's current position and returns the greedy next tokens (device
+    // int32 [batch]); positions advance by one.
+    torch::Tensor decode_step_batched(torch::Tensor tokens) {
+        if (tokens.numel() != batch_) throw std::runtime_error("tokens must have batch entries");
+        c10::cuda::CUDAGuard guard(device_);
+        tokens_.copy_(tokens.to(torch::kInt32).view({batch_}), true);
+        return step(false).clone();
+    }
+
     // Runs n steps and returns the generated tokens [n, batch] (device).
     torch::Tensor generate(int n) {
         c10::cuda::CUDAGuard guard(device_);
@@ -812,6 +822,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("set_state", &MegakernelBatchDecoder::set_state)
         .def("step", &MegakernelBatchDecoder::step, py::arg("with_logits") = false)
         .def("generate", &MegakernelBatchDecoder::generate)
+        .def("decode_step_batched", &MegakernelBatchDecoder::decode_step_batched)
         .def("check", &MegakernelBatchDecoder::check)
         .def("tokens", &MegakernelBatchDecoder::tokens)
         .def("positions", &MegakernelBatchDecoder::positions)

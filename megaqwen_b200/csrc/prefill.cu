@@ -293,6 +293,30 @@ void launch_prefill_float(const int* input_token_ids, int* output_token_id, int 
     g_pf_last_error = mq::prefill_forward(&p, stream);
 }
 
+void launch_prefill_megakernel(const int* token_ids, int* output_token_id, int seq_len, const void* embed_weight,
+                               const PrefillLayerWeights* layer_weights, const void* final_norm_weight,
+                               const void* lm_head_weight, const void* cos_table, const void* sin_table,
+                               void* k_cache, void* v_cache, void* /*hidden*/, void* /*residual*/,
+                               void* /*normalized*/, void* /*q_proj*/, void* /*k_proj*/, void* /*v_proj*/,
+                               void* /*attn_out*/, void* /*mlp_intermediate*/, void* /*final_hidden*/,
+                               void* /*hidden_bf16_out*/, void* /*block_max_vals*/, void* /*block_max_idxs*/,
+                               int num_layers, int max_seq_len, float attn_scale, cudaStream_t stream) {
+    // The reference passes a DEVICE array of layer pointers here (unlike
+    // launch_prefill_float); the engine reads the pointers on the host.
+    if (num_layers < 1 || num_layers > MQ_MAX_LAYERS || !layer_weights) { g_pf_last_error = MQ_ERR_INVALID_ARGUMENT; return; }
+    PrefillLayerWeights host[MQ_MAX_LAYERS];
+    if (cudaMemcpyAsync(host, layer_weights, sizeof(PrefillLayerWeights) * num_layers, cudaMemcpyDeviceToHost,
+                        stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess) {
+        g_pf_last_error = MQ_ERR_CUDA;
+        return;
+    }
+    launch_prefill_float(token_ids, output_token_id, seq_len, embed_weight, host, final_norm_weight, lm_head_weight,
+                         cos_table, sin_table, k_cache, v_cache, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                         nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr,
+                         nullptr, num_layers, max_seq_len, attn_scale, nullptr, stream);
+}
+
 int mq_prefill_get_last_error(void) { return g_pf_last_error; }
 
 }  // extern "C"

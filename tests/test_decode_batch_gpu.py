@@ -139,3 +139,21 @@ def test_batch_rejects_bad_state():
         bd.set_state(torch.tensor([1, 2, 3, 4]), torch.tensor([0, 0, 0, 32]))
     with pytest.raises(RuntimeError):
         bd.set_state(torch.tensor([1, 2]), torch.zeros(2))
+
+
+def test_decode_step_batched_entrypoint():
+    """decode_step_batched(tokens) -> next tokens, the additive batch
+    entrypoint, equals set_state + step on a second decoder."""
+    L, MS, B = 2, 64, 16
+    a = make_batch(L, MS, B, use_graph=True)
+    b = make_batch(L, MS, B, use_graph=False)
+    toks = torch.arange(B, dtype=torch.int32) * 1000 + 3
+    a.set_state(toks, torch.zeros(B))
+    b.set_state(toks, torch.zeros(B))
+    for step in range(5):
+        out_a = a.decode_step_batched(toks.cuda())
+        b.set_state(toks, torch.full((B,), step))
+        out_b = b.step(False).clone()
+        assert torch.equal(out_a.cpu(), out_b.cpu())
+        toks = out_a.cpu()
+    assert a.positions().cpu().tolist() == [5] * B

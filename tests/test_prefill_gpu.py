@@ -112,3 +112,34 @@ def test_reference_launch_prefill_float_abi():
     dec = make_decoder(L, MS, cls="MegakernelPrefillDecoder", max_prefill_len=S)
     assert int(out.item()) == dec.prefill_step(ids.cpu())
     assert torch.equal(kc[:, :, :S], dec.get_k_cache()[:, :, :S])
+
+
+def test_reference_launch_prefill_megakernel_abi():
+    """launch_prefill_megakernel (the reference's short-prompt launcher: DEVICE
+    layer table, fp32 scratch accepted and ignored) gives the prefill
+    decoder's token and cache rows."""
+    from megaqwen_b200.build import LIB
+    from megaqwen_b200.weights import LAYER_KEYS, rope_tables, seeded_prompt
+    lib = ctypes.CDLL(str(LIB))
+    L, S, MS = 2, 48, 64
+    _, wd = dev_weights(L)
+    cos, sin = rope_tables(MS, device="cuda")
+    ids = seeded_prompt(S, seed=8).cuda()
+    table = torch.tensor([wd.layers[i][k].data_ptr() for i in range(L) for k in LAYER_KEYS], dtype=torch.int64,
+                         device="cuda")
+    kc = torch.zeros(L, 8, MS, 128, dtype=torch.bfloat16, device="cuda")
+    vc = torch.zeros_like(kc)
+    out = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    V = ctypes.c_void_p
+    lib.launch_prefill_megakernel.argtypes = [V, V, ctypes.c_int] + [V] * 8 + [V] * 12 + \
+        [ctypes.c_int, ctypes.c_int, ctypes.c_float, V]
+    lib.launch_prefill_megakernel(ids.data_ptr(), out.data_ptr(), S, wd.embed.data_ptr(), table.data_ptr(),
+                                  wd.final_norm.data_ptr(), wd.lm_head.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+                                  kc.data_ptr(), vc.data_ptr(), *([None] * 12), L, MS, 128 ** -0.5,
+                                  torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert lib.mq_prefill_get_last_error() == 0
+    dec = make_decoder(L, MS, cls="MegakernelFusedPrefillDecoder", max_prefill_len=S)
+    assert int(out.item()) == dec.prefill_step(ids.cpu())
+    assert torch.equal(kc[:, :, :S], dec.get_k_cache()[:, :, :S])
+    assert torch.equal(vc[:, :, :S], dec.get_v_cache()[:, :, :S])
