@@ -220,6 +220,41 @@ def time_device_steps(dec, tok_buf, steps):
     return t_start.elapsed_time(t_end)
 
 
+def run_prefill(args, w, cos, sin, dev):
+    """Prefill (config 4): batch 1 and 8, 2048-token prompts, tensor-core path."""
+    import megaqwen_b200
+    from megaqwen_b200.weights import seeded_prompt
+    sweep_prefill = {}
+    peak_tf, peak_kind = measured_bf16_tflops()
+    for B in args.prefill_batches:
+        S = 2048
+        ids = torch.stack([seeded_prompt(S, seed=4 + b) for b in range(B)]).to(dev)
+        kc = torch.zeros(B, 28, 8, S + 8, 128, dtype=torch.bfloat16, device=dev)
+        vc = torch.zeros_like(kc)
+        wsb = torch.empty(megaqwen_b200._C.prefill_workspace_bytes(B, S), dtype=torch.uint8, device=dev)
+        run = lambda: megaqwen_b200._C.prefill_batch(w.embed, w.layer_weights_flat(), w.final_norm, w.lm_head,
+                                                     cos, sin, ids, kc, vc, None, wsb)  # noqa: E731
+        for _ in range(2):
+            run()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = args.prefill_reps
+        e0.record()
+        for _ in range(reps):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        flops = prefill_flops(B, S)
+        sweep_prefill[f"B{B}_S{S}"] = {"tok_s": round(B * S / (ms / 1000.0), 1), "ms": round(ms, 3),
+                                       "tflops": round(flops / (ms / 1000.0) / 1e12, 1),
+                                       "frac_of_bf16_peak": round(flops / (ms / 1000.0) / 1e12 / peak_tf, 4),
+                                       "peak_tflops": peak_tf, "peak_kind": peak_kind}
+        del kc, vc, wsb
+        torch.cuda.empty_cache()
+    return sweep_prefill
+
+
 def run_batch(args, w, cos, sin, dev, hbm, world):
     """Batched decode (config 5): per batch size and start position, graph-replayed
     steps over B sequences whose caches are pre-filled with N(0,1) bf16 K/V."""
@@ -273,6 +308,12 @@ def run_ours(args, rank, world, local):
     dec = megaqwen_b200.MegakernelDecoder(w.embed, w.layer_weights_flat(), w.final_norm, w.lm_head, cos, sin, 28,
                                           max_pos + 8)
     prompt = seeded_prompt(16).tolist()
+    if args.only_prefill:
+        # profiling entry: only the prefill measurements, one JSON line
+        res = run_prefill(args, w, cos, sin, dev)
+        if rank == 0:
+            print(json.dumps({"prefill": res}), flush=True)
+        return
     if args.only_batch:
         # profiling entry: only the batched-decode measurements, one JSON line
         batch = run_batch(args, w, cos, sin, dev, hbm, world)
@@ -338,35 +379,7 @@ def run_ours(args, rank, world, local):
             pm = P + 3 + n // 2
             sweep[str(P)] = {"tok_s": round(n / (tot / 1000.0), 1),
                              "roofline_frac": round(bytes_per_token(pm) / (lm / 1000.0) / 1e9 / hbm, 4)}
-        # prefill (config 4): batch 1 and 8, 2048-token prompts, tensor-core path
-        sweep_prefill = {}
-        peak_tf, peak_kind = measured_bf16_tflops()
-        for B in (1, 8):
-            S = 2048
-            ids = torch.stack([seeded_prompt(S, seed=4 + b) for b in range(B)]).to(dev)
-            kc = torch.zeros(B, 28, 8, S + 8, 128, dtype=torch.bfloat16, device=dev)
-            vc = torch.zeros_like(kc)
-            wsb = torch.empty(megaqwen_b200._C.prefill_workspace_bytes(B, S), dtype=torch.uint8, device=dev)
-            run = lambda: megaqwen_b200._C.prefill_batch(w.embed, w.layer_weights_flat(), w.final_norm, w.lm_head,
-                                                         cos, sin, ids, kc, vc, None, wsb)  # noqa: E731
-            for _ in range(2):
-                run()
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            reps = 3
-            e0.record()
-            for _ in range(reps):
-                run()
-            e1.record()
-            torch.cuda.synchronize()
-            ms = e0.elapsed_time(e1) / reps
-            flops = prefill_flops(B, S)
-            sweep_prefill[f"B{B}_S{S}"] = {"tok_s": round(B * S / (ms / 1000.0), 1), "ms": round(ms, 3),
-                                           "tflops": round(flops / (ms / 1000.0) / 1e12, 1),
-                                           "frac_of_bf16_peak": round(flops / (ms / 1000.0) / 1e12 / peak_tf, 4),
-                                           "peak_tflops": peak_tf, "peak_kind": peak_kind}
-            del kc, vc, wsb
-            torch.cuda.empty_cache()
+        sweep_prefill = run_prefill(args, w, cos, sin, dev)
     else:
         sweep_prefill = None
 
@@ -419,6 +432,9 @@ def main():
     ap.add_argument("--batch-steps", type=int, default=32)
     ap.add_argument("--batch-positions", type=lambda s: [int(x) for x in s.split(",") if x], default=[16, 1024])
     ap.add_argument("--only-batch", action="store_true", help="run only the batched-decode measurements")
+    ap.add_argument("--only-prefill", action="store_true", help="run only the prefill measurements")
+    ap.add_argument("--prefill-batches", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 8])
+    ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     args = ap.parse_args()
