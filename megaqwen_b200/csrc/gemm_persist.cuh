@@ -1,0 +1,338 @@
+// Persistent tcgen05 GEMM for prefill: C[M, N] = A[M, K] . B[N, K]^T, bf16
+// operands (both K-major), fp32 accumulation in TMEM, fused epilogues.
+//
+// One CTA per SM walks the 128 x 128 output tiles t = blockIdx.x, + gridDim.x ..
+// Warp 0 (one thread) streams A/B K-slices of 64 through an mbarrier ring with
+// TMA; warp 1 owns TMEM and one of its threads issues the MMAs; warps 2-5 run
+// the epilogue.  The accumulator is double-buffered in TMEM, so the epilogue
+// of tile i overlaps the MMAs of tile i + 1 and the loads run ahead across
+// tile boundaries.  Every wait is bounded and sets an error code.
+//
+// B may be up to three matrices side by side (q | k | v): tile columns
+// [0, nb0) read map 0, [nb0, nb0 + nb1) map 1, the rest map 2.  EPI_SILU_MUL
+// reads gate (map 0) and up (map 1) for the same tile into two accumulators.
+//
+// EPI_QKV (prefill QKV projection): one 128-column tile is one head.  q and k
+// heads get RMSNorm over the head (x norm weight) and rotate-half RoPE at the
+// row's position, in the thread that owns the row (no cross-thread traffic);
+// q goes to Qb, k and v to Kb / Vb and to the sequence's K/V cache (bf16).
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "gemm_tc.cuh"
+
+namespace mq {
+
+constexpr int EPI_QKV = 4;
+
+template <int EPI>
+struct PCfg {
+    static constexpr int NB = (EPI == EPI_SILU_MUL) ? 2 : 1;          // B tiles per stage
+    static constexpr int STAGE = GEMM_TILE_BYTES * (1 + NB);
+    static constexpr int NSTAGES = (EPI == EPI_SILU_MUL) ? 4 : 6;
+    static constexpr int ACC_COLS = GEMM_BN * NB;                     // one accumulator buffer
+    static constexpr int TMEM_COLS = 2 * ACC_COLS;                    // double-buffered
+    static constexpr int SMEM = NSTAGES * STAGE + 1024 + 256;
+};
+
+struct QkvPrefillEpi {
+    const __nv_bfloat16* q_norm;
+    const __nv_bfloat16* k_norm;
+    const __nv_bfloat16* cos_table;   // [max_seq, 128]
+    const __nv_bfloat16* sin_table;
+    __nv_bfloat16* Qb;                // [M, 2048]
+    __nv_bfloat16* Kb;                // [M, 1024]
+    __nv_bfloat16* Vb;                // [M, 1024]
+    __nv_bfloat16* k_cache;           // layer base of sequence 0: [8, max_seq, 128]
+    __nv_bfloat16* v_cache;
+    long long cache_seq_stride;       // elements between sequences' caches
+    int S, start_pos, max_seq;
+};
+
+struct PArgs {
+    void* C;             // output (fp32 or bf16, see epilogue)
+    int ldc;             // elements
+    int M, K;
+    int tiles_m, tiles_n;
+    int nb0, nb1;        // tile columns of B maps 0 and 1
+    QkvPrefillEpi qkv;
+    int* err;
+    long long timeout_cycles;
+};
+
+__device__ __forceinline__ uint4 pack8_bf16(const float* v) {
+    uint4 pk;
+    __nv_bfloat162 b0 = __floats2bfloat162_rn(v[0], v[1]);
+    __nv_bfloat162 b1 = __floats2bfloat162_rn(v[2], v[3]);
+    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[4], v[5]);
+    __nv_bfloat162 b3 = __floats2bfloat162_rn(v[6], v[7]);
+    pk.x = *reinterpret_cast<uint32_t*>(&b0);
+    pk.y = *reinterpret_cast<uint32_t*>(&b1);
+    pk.z = *reinterpret_cast<uint32_t*>(&b2);
+    pk.w = *reinterpret_cast<uint32_t*>(&b3);
+    return pk;
+}
+
+// QK-norm + RoPE (q, k heads) or plain rounding (v heads) of one row of one
+// head from the accumulator, written as bf16 to the operand buffer and, for k
+// and v, to the cache.  map: 0 q, 1 k, 2 v; head within the map.  Every lane
+// of the warp calls it (the TMEM loads are warp-collective); lanes whose row
+// is past M store nothing.
+__device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, int map, int head, int row_in) {
+    const QkvPrefillEpi& e = a.qkv;
+    const bool valid = row_in < a.M;
+    const int row = valid ? row_in : 0;
+    const int b = row / e.S, p = e.start_pos + (row - b * e.S);
+    __nv_bfloat16* dst = map == 0 ? e.Qb + (size_t)row * 2048 + head * 128
+                                  : (map == 1 ? e.Kb : e.Vb) + (size_t)row * 1024 + head * 128;
+    __nv_bfloat16* cache = map == 0 ? nullptr
+                                    : (map == 1 ? e.k_cache : e.v_cache) + b * e.cache_seq_stride +
+                                          ((size_t)head * e.max_seq + p) * 128;
+    if (map == 2) {
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+            float v[32];
+            tmem_ld32(acc + c, v);
+            if (valid) {
+#pragma unroll
+                for (int i = 0; i < 32; i += 8) {
+                    const uint4 pk = pack8_bf16(v + i);
+                    *reinterpret_cast<uint4*>(dst + c + i) = pk;
+                    *reinterpret_cast<uint4*>(cache + c + i) = pk;
+                }
+            }
+        }
+        return;
+    }
+    float ss = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 32) {
+        float v[32];
+        tmem_ld32(acc + c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+    }
+    const float r = rsqrtf(ss / 128.f + 1e-6f);
+    const __nv_bfloat16* nw = map == 0 ? e.q_norm : e.k_norm;
+    const __nv_bfloat16* cs = e.cos_table + (size_t)p * 128;
+    const __nv_bfloat16* sn = e.sin_table + (size_t)p * 128;
+    // rotate-half pairs (d, d + 64): chunk c with chunk c + 64
+#pragma unroll 1
+    for (int c = 0; c < 64; c += 32) {
+        float x1[32], x2[32];
+        tmem_ld32(acc + c, x1);
+        tmem_ld32(acc + c + 64, x2);
+        float o1[32], o2[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int d = c + i;
+            const float a1 = x1[i] * r * __bfloat162float(nw[d]);
+            const float a2 = x2[i] * r * __bfloat162float(nw[d + 64]);
+            o1[i] = a1 * __bfloat162float(cs[d]) - a2 * __bfloat162float(sn[d]);
+            o2[i] = a2 * __bfloat162float(cs[d + 64]) + a1 * __bfloat162float(sn[d + 64]);
+        }
+        if (!valid) continue;
+#pragma unroll
+        for (int i = 0; i < 32; i += 8) {
+            const uint4 p1 = pack8_bf16(o1 + i), p2 = pack8_bf16(o2 + i);
+            *reinterpret_cast<uint4*>(dst + c + i) = p1;
+            *reinterpret_cast<uint4*>(dst + c + 64 + i) = p2;
+            if (map == 1) {
+                *reinterpret_cast<uint4*>(cache + c + i) = p1;
+                *reinterpret_cast<uint4*>(cache + c + 64 + i) = p2;
+            }
+        }
+    }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
+                    const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
+                    const PArgs args) {
+    using Cfg = PCfg<EPI>;
+    extern __shared__ uint8_t persist_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(persist_smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::NSTAGES * Cfg::STAGE);
+    uint64_t* empty = full + Cfg::NSTAGES;
+    uint64_t* accf = empty + Cfg::NSTAGES;      // [2] MMA -> epilogue
+    uint64_t* acce = accf + 2;                  // [2] epilogue -> MMA
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ntiles = args.tiles_m * args.tiles_n;
+    const int nk = args.K / GEMM_BK;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < Cfg::NSTAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&accf[b], 1);
+            mbar_init(&acce[b], 4);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmA);
+        prefetch_tmap(&tmB0);
+        prefetch_tmap(&tmB1);
+        prefetch_tmap(&tmB2);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, Cfg::TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t g = 0;   // k-blocks issued so far (ring position)
+            for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+                const int m0 = (t / args.tiles_n) * GEMM_BM;
+                int nt = t % args.tiles_n;
+                const CUtensorMap* tb = &tmB0;
+                if (EPI != EPI_SILU_MUL && nt >= args.nb0) {
+                    nt -= args.nb0;
+                    tb = &tmB1;
+                    if (nt >= args.nb1) {
+                        nt -= args.nb1;
+                        tb = &tmB2;
+                    }
+                }
+                const int n0 = nt * GEMM_BN;
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const uint32_t s = g % Cfg::NSTAGES;
+                    if (g >= (uint32_t)Cfg::NSTAGES &&
+                        !bounded_wait(&empty[s], ((g / Cfg::NSTAGES) & 1) ^ 1, args.timeout_cycles)) {
+                        *abort_flag = 1;
+                        atomicExch(args.err, 31);
+                        break;
+                    }
+                    uint8_t* st = smem + s * Cfg::STAGE;
+                    mbar_arrive_expect_tx(&full[s], Cfg::STAGE);
+                    tma_load_2d(st, &tmA, kb * GEMM_BK, m0, &full[s]);
+                    tma_load_2d(st + GEMM_TILE_BYTES, tb, kb * GEMM_BK, n0, &full[s]);
+                    if (Cfg::NB == 2) tma_load_2d(st + 2 * GEMM_TILE_BYTES, &tmB1, kb * GEMM_BK, n0, &full[s]);
+                }
+            }
+            // on an abort every copy still in flight lands before the CTA may exit
+            if (*abort_flag)
+                for (uint32_t q = g > (uint32_t)Cfg::NSTAGES ? g - Cfg::NSTAGES : 0; q < g; ++q)
+                    bounded_wait(&full[q % Cfg::NSTAGES], (q / Cfg::NSTAGES) & 1, args.timeout_cycles);
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, GEMM_BN);
+            uint32_t g = 0;
+            int i = 0;
+            for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++i) {
+                const int b = i & 1, u = i >> 1;
+                if (u >= 1 && !bounded_wait(&acce[b], (u - 1) & 1, args.timeout_cycles)) {
+                    *abort_flag = 1;
+                    atomicExch(args.err, 32);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(b * Cfg::ACC_COLS);
+                for (int kb = 0; kb < nk; ++kb, ++g) {
+                    const uint32_t s = g % Cfg::NSTAGES;
+                    if (!bounded_wait(&full[s], (g / Cfg::NSTAGES) & 1, args.timeout_cycles) || *abort_flag) {
+                        *abort_flag = 1;
+                        atomicExch(args.err, 33);
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_u32(smem + s * Cfg::STAGE);
+#pragma unroll
+                    for (int k = 0; k < GEMM_BK / 16; ++k) {
+                        const uint64_t ad = sw128_kmajor_desc(sa + k * 32);
+                        tc_mma_f16(acc, ad, sw128_kmajor_desc(sa + GEMM_TILE_BYTES + k * 32), idesc, (kb | k) != 0);
+                        if (Cfg::NB == 2)
+                            tc_mma_f16(acc + GEMM_BN, ad, sw128_kmajor_desc(sa + 2 * GEMM_TILE_BYTES + k * 32), idesc,
+                                       (kb | k) != 0);
+                    }
+                    tc_commit(&empty[s]);
+                }
+                tc_commit(&accf[b]);   // also after an abort: arrives once the issued MMAs are done
+            }
+        }
+    } else {
+        // epilogue: warp w covers TMEM lanes 32 * (w % 4) .. + 31 (row of the tile)
+        const int quad = warp & 3;
+        int i = 0;
+        for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
+            const int b = i & 1, u = i >> 1;
+            if (!bounded_wait(&accf[b], u & 1, args.timeout_cycles) || *abort_flag) {
+                if (lane == 0) atomicExch(args.err, 34);
+                *abort_flag = 1;
+                break;
+            }
+            tc_fence_after();
+            const int m0 = (t / args.tiles_n) * GEMM_BM;
+            const int nt_all = t % args.tiles_n;
+            const int row = m0 + quad * 32 + lane;
+            const uint32_t acc = tmem + (uint32_t)(b * Cfg::ACC_COLS) + ((uint32_t)(quad * 32) << 16);
+            if (EPI == EPI_QKV) {
+                int map = 0, head = nt_all;
+                if (head >= args.nb0) {
+                    head -= args.nb0;
+                    map = 1;
+                    if (head >= args.nb1) {
+                        head -= args.nb1;
+                        map = 2;
+                    }
+                }
+                qkv_row_epilogue(args, acc, map, head, row);
+            } else {
+                const int n0 = nt_all * GEMM_BN;
+                for (int c = 0; c < GEMM_BN; c += 32) {
+                    float v[32];
+                    tmem_ld32(acc + c, v);
+                    if (EPI == EPI_SILU_MUL) {
+                        float up[32];
+                        tmem_ld32(acc + GEMM_BN + c, up);
+#pragma unroll
+                        for (int q = 0; q < 32; ++q) v[q] = v[q] / (1.0f + expf(-v[q])) * up[q];
+                    }
+                    if (row < args.M) {
+                        if (EPI == EPI_STORE_F32 || EPI == EPI_ADD_F32) {
+                            float* out = reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + n0 + c;
+#pragma unroll
+                            for (int q = 0; q < 32; q += 4) {
+                                float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+                                if (EPI == EPI_ADD_F32) {
+                                    const float4 p = *reinterpret_cast<const float4*>(out + q);
+                                    o.x += p.x; o.y += p.y; o.z += p.z; o.w += p.w;
+                                }
+                                *reinterpret_cast<float4*>(out + q) = o;
+                            }
+                        } else {
+                            __nv_bfloat16* out =
+                                reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + n0 + c;
+#pragma unroll
+                            for (int q = 0; q < 32; q += 8) *reinterpret_cast<uint4*>(out + q) = pack8_bf16(v + q);
+                        }
+                    }
+                }
+            }
+            // this warp's lanes have read the buffer: hand it back to the MMA thread
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    }
+}
+
+}  // namespace mq

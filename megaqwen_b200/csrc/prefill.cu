@@ -10,6 +10,7 @@
 #include <mutex>
 
 #include "gemm_tc.cuh"
+#include "gemm_persist.cuh"
 #include "megaqwen_b200.h"
 
 namespace mq {
@@ -46,35 +47,59 @@ bool make_tmap(CUtensorMap* map, const void* ptr, uint64_t rows, uint64_t cols, 
 
 namespace {
 
+int num_sms() {
+    static int sms[64] = {0};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return 148;
+    if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    return sms[dev] > 0 ? sms[dev] : 148;
+}
+
+// One persistent GEMM launch: A [M, K] against up to three B maps side by side
+// (Nmap[i] rows each; EPI_SILU_MUL: gate, up), one CTA per SM.
 template <int EPI>
-int launch_gemm(const void* A, int lda, const void* B, int ldb, const void* B2, void* C, int ldc, int M, int N,
-                int K, int* err, cudaStream_t stream) {
-    using Cfg = GemmCfg<EPI>;
+int launch_persist(const void* A, int lda, const void* const* Bm, const int* Nmap, int nmaps, int ldb, void* C, int ldc,
+                   int M, int K, const QkvPrefillEpi* qkv, int* err, cudaStream_t stream) {
+    using Cfg = PCfg<EPI>;
     static bool configured[64] = {false};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return MQ_ERR_CUDA;
     if (dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(gemm_tc_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
+        if (cudaFuncSetAttribute(gemm_persist_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
             cudaSuccess)
             return MQ_ERR_CUDA;
         configured[dev] = true;
     }
-    CUtensorMap ta, tb, tb2;
+    CUtensorMap ta, tb[3];
     if (!make_tmap(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, GEMM_BM)) return MQ_ERR_CUDA;
-    if (!make_tmap(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, GEMM_BN)) return MQ_ERR_CUDA;
-    tb2 = tb;
-    if (EPI == EPI_SILU_MUL && !make_tmap(&tb2, B2, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, GEMM_BN)) return MQ_ERR_CUDA;
-    GemmArgs a;
+    for (int i = 0; i < 3; ++i) {
+        const int m = i < nmaps ? i : nmaps - 1;
+        if (!make_tmap(&tb[i], Bm[m], (uint64_t)Nmap[m], (uint64_t)K, (uint64_t)ldb, GEMM_BN)) return MQ_ERR_CUDA;
+    }
+    PArgs a = {};
     a.C = C;
     a.ldc = ldc;
     a.M = M;
-    a.N = N;
     a.K = K;
+    a.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
+    a.nb0 = Nmap[0] / GEMM_BN;
+    a.nb1 = nmaps > 1 ? Nmap[1] / GEMM_BN : 0;
+    a.tiles_n = EPI == EPI_SILU_MUL ? a.nb0 : a.nb0 + a.nb1 + (nmaps > 2 ? Nmap[2] / GEMM_BN : 0);
+    if (qkv) a.qkv = *qkv;
     a.err = err;
     a.timeout_cycles = 4000000000ll;  // ~2 s at 1.9 GHz
-    dim3 grid(N / GEMM_BN, (M + GEMM_BM - 1) / GEMM_BM);
-    gemm_tc_kernel<EPI><<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, tb2, a);
+    const int ntiles = a.tiles_m * a.tiles_n;
+    const int grid = ntiles < num_sms() ? ntiles : num_sms();
+    gemm_persist_kernel<EPI><<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb[0], tb[1], tb[2], a);
     return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+}
+
+template <int EPI>
+int launch_gemm(const void* A, int lda, const void* B, int ldb, const void* B2, void* C, int ldc, int M, int N,
+                int K, int* err, cudaStream_t stream) {
+    const void* Bm[2] = {B, B2 ? B2 : B};
+    const int Nm[2] = {N, N};
+    return launch_persist<EPI>(A, lda, Bm, Nm, EPI == EPI_SILU_MUL ? 2 : 1, ldb, C, ldc, M, K, nullptr, err, stream);
 }
 
 }  // namespace
@@ -113,7 +138,7 @@ namespace mq {
 namespace {
 
 struct PrefillLayout {
-    size_t X, Xn, QKV, Qb, Kb, Vb, Ob, act, lastn, logits, err, total;
+    size_t X, Xn, Qb, Kb, Vb, Ob, act, lastn, logits, err, total;
 };
 
 PrefillLayout prefill_layout(int B, int S) {
@@ -123,7 +148,6 @@ PrefillLayout prefill_layout(int B, int S) {
     auto take = [&](size_t bytes) { size_t r = o; o += (bytes + 255) & ~size_t(255); return r; };
     L.X = take(M * 1024 * 4);
     L.Xn = take(M * 1024 * 2);
-    L.QKV = take(M * 4096 * 4);
     L.Qb = take(M * 2048 * 2);
     L.Kb = take(M * 1024 * 2);
     L.Vb = take(M * 1024 * 2);
@@ -156,7 +180,6 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
     uint8_t* ws = (uint8_t*)p->workspace;
     float* X = (float*)(ws + L.X);
     pf::bf16* Xn = (pf::bf16*)(ws + L.Xn);
-    float* QKV = (float*)(ws + L.QKV);
     pf::bf16* Qb = (pf::bf16*)(ws + L.Qb);
     pf::bf16* Kb = (pf::bf16*)(ws + L.Kb);
     pf::bf16* Vb = (pf::bf16*)(ws + L.Vb);
@@ -183,30 +206,27 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
     for (int l = 0; l < p->num_layers; ++l) {
         const LDGLayerWeights& W = p->layers_host[l];
         pf::rmsnorm_bf16_kernel<<<(M + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)W.input_layernorm_weight, Xn, M, 1, 0);
-        MQ_TRY(gemm_bf16(Xn, 1024, W.q_proj_weight, 1024, nullptr, QKV, 4096, M, 2048, 1024, EPI_STORE_F32, err, st));
-        MQ_TRY(gemm_bf16(Xn, 1024, W.k_proj_weight, 1024, nullptr, QKV + 2048, 4096, M, 1024, 1024, EPI_STORE_F32, err,
-                         st));
-        MQ_TRY(gemm_bf16(Xn, 1024, W.v_proj_weight, 1024, nullptr, QKV + 3072, 4096, M, 1024, 1024, EPI_STORE_F32, err,
-                         st));
-        pf::QkvArgs qa;
-        qa.qkv = QKV;
-        qa.q_norm = (const pf::bf16*)W.q_norm_weight;
-        qa.k_norm = (const pf::bf16*)W.k_norm_weight;
-        qa.cos_table = (const pf::bf16*)p->cos_table;
-        qa.sin_table = (const pf::bf16*)p->sin_table;
-        qa.Qb = Qb;
-        qa.Kb = Kb;
-        qa.Vb = Vb;
-        const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * MQ_HEAD_DIM;
-        qa.k_cache = (pf::bf16*)p->k_cache + layer_off;
-        qa.v_cache = (pf::bf16*)p->v_cache + layer_off;
-        qa.cache_seq_stride = p->cache_seq_stride;
-        qa.S = S;
-        qa.start_pos = 0;
-        qa.max_seq_len = p->max_seq_len;
-        qa.pos_dev = nullptr;
-        qa.Qf = nullptr;
-        pf::qknorm_rope_kernel<<<M, 1024, 0, st>>>(qa);
+        {
+            // q | k | v projections with QK-norm, RoPE and the K/V cache write in the epilogue
+            QkvPrefillEpi e;
+            e.q_norm = (const pf::bf16*)W.q_norm_weight;
+            e.k_norm = (const pf::bf16*)W.k_norm_weight;
+            e.cos_table = (const pf::bf16*)p->cos_table;
+            e.sin_table = (const pf::bf16*)p->sin_table;
+            e.Qb = Qb;
+            e.Kb = Kb;
+            e.Vb = Vb;
+            const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * MQ_HEAD_DIM;
+            e.k_cache = (pf::bf16*)p->k_cache + layer_off;
+            e.v_cache = (pf::bf16*)p->v_cache + layer_off;
+            e.cache_seq_stride = p->cache_seq_stride;
+            e.S = S;
+            e.start_pos = 0;
+            e.max_seq = p->max_seq_len;
+            const void* Bm[3] = {W.q_proj_weight, W.k_proj_weight, W.v_proj_weight};
+            const int Nm[3] = {2048, 1024, 1024};
+            MQ_TRY(launch_persist<EPI_QKV>(Xn, 1024, Bm, Nm, 3, 1024, nullptr, 0, M, 1024, &e, err, st));
+        }
         dim3 fgrid((S + pf::FA_B - 1) / pf::FA_B, MQ_NUM_Q_HEADS, B);
         pf::flash_attn_causal_kernel<<<fgrid, 128, pf::FA_SMEM, st>>>(Qb, Kb, Vb, Ob, S, scale_log2);
         MQ_TRY(gemm_bf16(Ob, 2048, W.o_proj_weight, 2048, nullptr, X, 1024, M, 1024, 2048, EPI_ADD_F32, err, st));
