@@ -4,7 +4,8 @@
 // Q [M, 16*128], K/V [M, 8*128] bf16 rows m = b*S + s; O [M, 16*128] bf16.
 // One CTA = (query block of 64, q head, sequence), 4 warps x 16 query rows.
 // Key/value blocks of 64 rows are staged in shared memory with rows padded to
-// 272 bytes so ldmatrix reads are bank-conflict free.  Scores are scaled in
+// 272 bytes so ldmatrix reads are bank-conflict free; they are double-buffered
+// with cp.async so block kb + 1 loads while block kb is computed.  Scores are scaled in
 // the log2 domain (exp2).  Heavier (later) query blocks are scheduled first.
 #pragma once
 
@@ -18,7 +19,7 @@ namespace pf {
 
 constexpr int FA_B = 64;          // query rows per CTA and keys per block
 constexpr int FA_LD = 136;        // padded row (elements)
-constexpr int FA_SMEM = 3 * FA_B * FA_LD * 2;   // Q, K, V tiles (dynamic shared memory)
+constexpr int FA_SMEM = 5 * FA_B * FA_LD * 2;   // Q tile + double-buffered K, V tiles (dynamic shared memory)
 
 __device__ __forceinline__ void ldm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -39,17 +40,23 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
     return *reinterpret_cast<uint32_t*>(&t);
 }
 
-// Copy rows [r0, r0+64) of a [.., ld]-strided bf16 matrix (128 columns starting
-// at col0) into padded shared memory; rows >= rmax are zero.
+// Asynchronously copy rows [r0, r0+64) of a [.., ld]-strided bf16 matrix (128
+// columns starting at col0) into padded shared memory (cp.async, 16 bytes per
+// copy); rows >= rmax are zero-filled.
 __device__ __forceinline__ void fa_load_tile(__nv_bfloat16* dst, const __nv_bfloat16* src, int ld, int col0, int r0,
                                              int rmax) {
     for (int i = threadIdx.x; i < FA_B * 16; i += blockDim.x) {
         const int r = i >> 4, c = (i & 15) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (r0 + r < rmax) v = *reinterpret_cast<const uint4*>(src + (size_t)(r0 + r) * ld + col0 + c);
-        *reinterpret_cast<uint4*>(dst + r * FA_LD + c) = v;
+        const bool ok = r0 + r < rmax;
+        const __nv_bfloat16* g = ok ? src + (size_t)(r0 + r) * ld + col0 + c : src;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst + r * FA_LD + c)), "l"(g),
+                     "r"(ok ? 16u : 0u)
+                     : "memory");
     }
 }
+__device__ __forceinline__ void fa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void fa_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 static __global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __nv_bfloat16* __restrict__ Q,
                                                                 const __nv_bfloat16* __restrict__ K,
@@ -58,8 +65,8 @@ static __global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __n
                                                                 float scale_log2) {
     extern __shared__ __align__(16) __nv_bfloat16 fa_smem[];
     __nv_bfloat16* sQ = fa_smem;
-    __nv_bfloat16* sK = sQ + FA_B * FA_LD;
-    __nv_bfloat16* sV = sK + FA_B * FA_LD;
+    __nv_bfloat16* sK0 = sQ + FA_B * FA_LD;       // K tiles [2], then V tiles [2]
+    __nv_bfloat16* sV0 = sK0 + 2 * FA_B * FA_LD;
     const int nqb = (S + FA_B - 1) / FA_B;
     const int qb = nqb - 1 - (int)blockIdx.x;
     const int h = blockIdx.y, b = blockIdx.z, kvh = h / (NQ / NKV);
@@ -67,15 +74,15 @@ static __global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __n
     const int g = lane >> 2, t = lane & 3;
     const int q0 = qb * FA_B;
     const size_t base = (size_t)b * S;
+    const __nv_bfloat16* Kg = K + base * (NKV * D);
+    const __nv_bfloat16* Vg = V + base * (NKV * D);
 
+    // Q and the first K/V tile in flight together; tile kb + 1 loads while kb computes
     fa_load_tile(sQ, Q + base * (NQ * D), NQ * D, h * D, q0, S);
-    __syncthreads();
+    fa_load_tile(sK0, Kg, NKV * D, kvh * D, 0, S);
+    fa_load_tile(sV0, Vg, NKV * D, kvh * D, 0, S);
+    fa_commit();
     uint32_t qf[8][4];
-#pragma unroll
-    for (int s = 0; s < 8; ++s)
-        ldm_x4(smem_u32(sQ + (warp * 16 + (lane & 15)) * FA_LD + s * 16 + (lane >> 4) * 8), qf[s][0], qf[s][1],
-               qf[s][2], qf[s][3]);
-
     float oacc[16][4];
 #pragma unroll
     for (int j = 0; j < 16; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
@@ -84,10 +91,24 @@ static __global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __n
 
     for (int kb = 0; kb <= qb; ++kb) {
         const int k0 = kb * FA_B;
+        if (kb + 1 <= qb) {
+            const int nb = (kb + 1) & 1;
+            fa_load_tile(sK0 + nb * FA_B * FA_LD, Kg, NKV * D, kvh * D, k0 + FA_B, S);
+            fa_load_tile(sV0 + nb * FA_B * FA_LD, Vg, NKV * D, kvh * D, k0 + FA_B, S);
+            fa_commit();
+            fa_wait<1>();
+        } else {
+            fa_wait<0>();
+        }
         __syncthreads();
-        fa_load_tile(sK, K + base * (NKV * D), NKV * D, kvh * D, k0, S);
-        fa_load_tile(sV, V + base * (NKV * D), NKV * D, kvh * D, k0, S);
-        __syncthreads();
+        if (kb == 0) {
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+                ldm_x4(smem_u32(sQ + (warp * 16 + (lane & 15)) * FA_LD + s * 16 + (lane >> 4) * 8), qf[s][0], qf[s][1],
+                       qf[s][2], qf[s][3]);
+        }
+        const __nv_bfloat16* sK = sK0 + (kb & 1) * FA_B * FA_LD;
+        const __nv_bfloat16* sV = sV0 + (kb & 1) * FA_B * FA_LD;
         float sacc[8][4];
 #pragma unroll
         for (int j = 0; j < 8; ++j) sacc[j][0] = sacc[j][1] = sacc[j][2] = sacc[j][3] = 0.f;
@@ -158,6 +179,7 @@ static __global__ void __launch_bounds__(128) flash_attn_causal_kernel(const __n
                 mma_bf16(oacc[2 * jj + 1], pa[kt], b2, b3);
             }
         }
+        __syncthreads();   // every warp is done with this buffer before it is refilled
     }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {

@@ -117,30 +117,45 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
     const __nv_bfloat16* nw = map == 0 ? e.q_norm : e.k_norm;
     const __nv_bfloat16* cs = e.cos_table + (size_t)p * 128;
     const __nv_bfloat16* sn = e.sin_table + (size_t)p * 128;
-    // rotate-half pairs (d, d + 64): chunk c with chunk c + 64
+    // rotate-half pairs (d, d + 64): chunk c with chunk c + 64; weights, cos and
+    // sin rows are read 8 bf16 at a time
 #pragma unroll 1
     for (int c = 0; c < 64; c += 32) {
         float x1[32], x2[32];
         tmem_ld32(acc + c, x1);
         tmem_ld32(acc + c + 64, x2);
-        float o1[32], o2[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-            const int d = c + i;
-            const float a1 = x1[i] * r * __bfloat162float(nw[d]);
-            const float a2 = x2[i] * r * __bfloat162float(nw[d + 64]);
-            o1[i] = a1 * __bfloat162float(cs[d]) - a2 * __bfloat162float(sn[d]);
-            o2[i] = a2 * __bfloat162float(cs[d + 64]) + a1 * __bfloat162float(sn[d + 64]);
-        }
-        if (!valid) continue;
 #pragma unroll
         for (int i = 0; i < 32; i += 8) {
-            const uint4 p1 = pack8_bf16(o1 + i), p2 = pack8_bf16(o2 + i);
-            *reinterpret_cast<uint4*>(dst + c + i) = p1;
-            *reinterpret_cast<uint4*>(dst + c + 64 + i) = p2;
-            if (map == 1) {
-                *reinterpret_cast<uint4*>(cache + c + i) = p1;
-                *reinterpret_cast<uint4*>(cache + c + 64 + i) = p2;
+            const int d = c + i;
+            const uint4 w1 = *reinterpret_cast<const uint4*>(nw + d), w2 = *reinterpret_cast<const uint4*>(nw + d + 64);
+            const uint4 c1 = *reinterpret_cast<const uint4*>(cs + d), c2 = *reinterpret_cast<const uint4*>(cs + d + 64);
+            const uint4 s1 = *reinterpret_cast<const uint4*>(sn + d), s2 = *reinterpret_cast<const uint4*>(sn + d + 64);
+            const uint32_t w1v[4] = {w1.x, w1.y, w1.z, w1.w}, w2v[4] = {w2.x, w2.y, w2.z, w2.w};
+            const uint32_t c1v[4] = {c1.x, c1.y, c1.z, c1.w}, c2v[4] = {c2.x, c2.y, c2.z, c2.w};
+            const uint32_t s1v[4] = {s1.x, s1.y, s1.z, s1.w}, s2v[4] = {s2.x, s2.y, s2.z, s2.w};
+            float o1[8], o2[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const int h = j >> 1;
+                const float nw1 = (j & 1) ? bf16hi(w1v[h]) : bf16lo(w1v[h]);
+                const float nw2 = (j & 1) ? bf16hi(w2v[h]) : bf16lo(w2v[h]);
+                const float cc1 = (j & 1) ? bf16hi(c1v[h]) : bf16lo(c1v[h]);
+                const float cc2 = (j & 1) ? bf16hi(c2v[h]) : bf16lo(c2v[h]);
+                const float ss1 = (j & 1) ? bf16hi(s1v[h]) : bf16lo(s1v[h]);
+                const float ss2 = (j & 1) ? bf16hi(s2v[h]) : bf16lo(s2v[h]);
+                const float a1 = x1[i + j] * r * nw1;
+                const float a2 = x2[i + j] * r * nw2;
+                o1[j] = a1 * cc1 - a2 * ss1;
+                o2[j] = a2 * cc2 + a1 * ss2;
+            }
+            if (valid) {
+                const uint4 p1 = pack8_bf16(o1), p2 = pack8_bf16(o2);
+                *reinterpret_cast<uint4*>(dst + d) = p1;
+                *reinterpret_cast<uint4*>(dst + d + 64) = p2;
+                if (map == 1) {
+                    *reinterpret_cast<uint4*>(cache + d) = p1;
+                    *reinterpret_cast<uint4*>(cache + d + 64) = p2;
+                }
             }
         }
     }
