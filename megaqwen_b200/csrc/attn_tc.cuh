@@ -1,0 +1,315 @@
+// Causal GQA flash attention for prefill on the 5th-generation tensor cores
+// (tcgen05, accumulators in TMEM).
+//
+// One CTA = (block of 128 query rows, q head, sequence); 192 threads:
+//   warp 0      TMA producer: Q once, then K and V^T tiles of 128 keys into a
+//               2-stage ring;
+//   warp 1      TMEM owner; one thread issues the MMAs:
+//                 S_j = Q K_j^T  (M=128 queries, N=128 keys, K=128 dims) into
+//                                 one of two S buffers,
+//                 O_j = P_j V_j  (M=128 queries, N=128 dims, K=128 keys) into
+//                                 the O buffer;
+//               S_{j+1} is issued before O_j so the tensor core works while
+//               the softmax warps are busy;
+//   warps 2-5   softmax and output, one query row per thread (TMEM lane):
+//               row max and exp2 of S_j in registers, P_j written as bf16 to
+//               shared memory in the 128-byte-swizzled K-major layout the MMA
+//               reads, and O_{j-1} folded into a register accumulator with
+//               the online-softmax correction.
+// All operands are K-major: Q [q][d], K [key][d], P [q][key] and V^T [d][key]
+// (the QKV GEMM epilogue writes V transposed per sequence and kv head).
+// Scores are in the log2 domain.  Every wait is bounded and sets an error code.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include "mq_tc.cuh"
+
+namespace mq {
+namespace fa {
+
+constexpr int BQ = 128;                     // query rows per CTA
+constexpr int BK = 128;                     // keys per tile
+constexpr int HD = 128;                     // head dim
+constexpr int ATOM = 128 * 128;             // bytes of a 128-row x 64-element swizzled atom (16 KB)
+constexpr int TILE = 2 * ATOM;              // a 128 x 128 bf16 operand (32 KB)
+constexpr int SM_Q = 0;
+constexpr int SM_K = SM_Q + TILE;           // [2] stages
+constexpr int SM_V = SM_K + 2 * TILE;       // [2] stages (V^T)
+constexpr int SM_P = SM_V + 2 * TILE;
+constexpr int SM_BAR = SM_P + TILE;
+constexpr int SMEM = SM_BAR + 256 + 1024;   // + barriers + alignment slack
+constexpr int THREADS = 192;
+
+struct Args {
+    __nv_bfloat16* O;       // [M, 2048] bf16, row m = b * S + s
+    int S;                  // sequence length
+    float scale_log2;
+    int* err;
+    long long timeout_cycles;
+};
+
+__device__ __forceinline__ bool fa_wait(uint64_t* bar, uint32_t parity, long long limit) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > limit) return false;
+    }
+    return true;
+}
+
+// tmQ: Qb [M, 2048]; tmK: Kb [M, 1024]; tmV: V^T [B * 8 * 128, ldv] (rows = (b * 8 + kvh) * 128 + d).
+__global__ void __launch_bounds__(THREADS, 1)
+fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+             const __grid_constant__ CUtensorMap tmV, const Args args) {
+    extern __shared__ uint8_t fa_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+    uint64_t* q_full = bars + 0;
+    uint64_t* kv_full = bars + 1;     // [2]
+    uint64_t* kv_empty = bars + 3;    // [2]
+    uint64_t* s_full = bars + 5;      // [2]
+    uint64_t* s_free = bars + 7;      // [2]
+    uint64_t* p_full = bars + 9;
+    uint64_t* o_full = bars + 10;
+    uint64_t* o_free = bars + 11;
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+    const int S = args.S;
+    const int nqb = (S + BQ - 1) / BQ;
+    const int qb = nqb - 1 - (int)blockIdx.x;   // heavier (later) query blocks first
+    const int h = blockIdx.y, b = blockIdx.z, kvh = h >> 1;
+    const int q0 = qb * BQ;
+    const int nt = qb + 1;                      // key tiles 0..qb (causal)
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long lim = args.timeout_cycles;
+
+    if (threadIdx.x == 0) {
+        mbar_init(q_full, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&kv_full[i], 1);
+            mbar_init(&kv_empty[i], 1);
+            mbar_init(&s_full[i], 1);
+            mbar_init(&s_free[i], 4);
+        }
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        mbar_init(o_free, 4);
+        *abort_flag = 0;
+        fence_mbar_init();
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_holder, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;       // S buffers at columns 0 / 128, O at 256
+
+    if (warp == 0) {
+        if (lane == 0) {
+            const int row0 = b * S;
+            mbar_arrive_expect_tx(q_full, TILE);
+            tma_load_2d(smem + SM_Q, &tmQ, h * HD, row0 + q0, q_full);
+            tma_load_2d(smem + SM_Q + ATOM, &tmQ, h * HD + 64, row0 + q0, q_full);
+            for (int j = 0; j < nt; ++j) {
+                const int st = j & 1, u = j >> 1;
+                if (u >= 1 && !fa_wait(&kv_empty[st], (u - 1) & 1, lim)) {
+                    *abort_flag = 1;
+                    atomicExch(args.err, 41);
+                    break;
+                }
+                if (*abort_flag) break;
+                uint8_t* kd = smem + SM_K + st * TILE;
+                uint8_t* vd = smem + SM_V + st * TILE;
+                mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
+                tma_load_2d(kd, &tmK, kvh * HD, row0 + j * BK, &kv_full[st]);
+                tma_load_2d(kd + ATOM, &tmK, kvh * HD + 64, row0 + j * BK, &kv_full[st]);
+                const int vrow = (b * 8 + kvh) * HD;
+                tma_load_2d(vd, &tmV, j * BK, vrow, &kv_full[st]);
+                tma_load_2d(vd + ATOM, &tmV, j * BK + 64, vrow, &kv_full[st]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = idesc_bf16_f32(BQ, BK);
+            const uint32_t sq = smem_u32(smem + SM_Q), sp = smem_u32(smem + SM_P);
+            bool ok = fa_wait(q_full, 0, lim);
+            // O_j = P_j V_j into the O buffer
+            auto pv = [&](int j) -> bool {
+                if (!fa_wait(p_full, j & 1, lim)) return false;
+                if (j >= 1 && !fa_wait(o_free, (j - 1) & 1, lim)) return false;
+                tc_fence_after();
+                const uint32_t sv = smem_u32(smem + SM_V + (j & 1) * TILE);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k) {
+                    const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
+                    tc_mma_f16(tmem + 256, sw128_kmajor_desc(sp + off), sw128_kmajor_desc(sv + off), idesc, k != 0);
+                }
+                tc_commit(o_full);
+                tc_commit(&kv_empty[j & 1]);
+                return true;
+            };
+            for (int j = 0; ok && j < nt; ++j) {
+                const int st = j & 1, u = j >> 1;
+                if (!fa_wait(&kv_full[st], u & 1, lim) || (u >= 1 && !fa_wait(&s_free[st], (u - 1) & 1, lim)) ||
+                    *abort_flag) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sk = smem_u32(smem + SM_K + st * TILE);
+#pragma unroll
+                for (int k = 0; k < HD / 16; ++k) {
+                    const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
+                    tc_mma_f16(tmem + st * BK, sw128_kmajor_desc(sq + off), sw128_kmajor_desc(sk + off), idesc,
+                               k != 0);
+                }
+                tc_commit(&s_full[st]);
+                if (j >= 1 && !pv(j - 1)) {
+                    ok = false;
+                    break;
+                }
+            }
+            if (ok && !pv(nt - 1)) ok = false;
+            if (!ok) {
+                *abort_flag = 1;
+                atomicExch(args.err, 42);
+            }
+        }
+    } else {
+        // softmax / output: thread = query row r of the block (TMEM lane r)
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const int qrow = q0 + r;
+        const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        float o[HD];
+#pragma unroll
+        for (int i = 0; i < HD; ++i) o[i] = 0.f;
+        float m = -INFINITY, l = 0.f, corr_prev = 1.f;
+        uint8_t* prow = smem + SM_P + r * 128;
+        bool ok = true;
+        for (int j = 0; j < nt; ++j) {
+            const int st = j & 1, u = j >> 1;
+            if (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t sa = tmem + lane_off + st * BK;
+            const int k0 = j * BK;
+            // pass 1: row max of the tile (scaled, causal and length masked)
+            float tmax = -INFINITY;
+#pragma unroll 1
+            for (int c = 0; c < BK; c += 32) {
+                float v[32];
+                tmem_ld32(sa + c, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int key = k0 + c + i;
+                    const float x = (key > qrow || key >= S) ? -INFINITY : v[i] * args.scale_log2;
+                    tmax = fmaxf(tmax, x);
+                }
+            }
+            const float mn = fmaxf(m, tmax);
+            const float corr = exp2f(m - mn);   // 0 on the first tile (m = -inf)
+            m = mn;
+            // fold O_{j-1} (relative to the previous max) before P_j overwrites P_{j-1}
+            if (j >= 1) {
+                if (!fa_wait(o_full, (j - 1) & 1, lim)) { ok = false; break; }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) {
+                    float v[32];
+                    tmem_ld32(tmem + lane_off + 256 + c, v);
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * corr_prev + v[i];
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_free);
+            }
+            // pass 2: P = exp2(s - m) as bf16 into the swizzled P tile, row sum
+            float psum = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < BK; c += 32) {
+                float v[32];
+                tmem_ld32(sa + c, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const int key = k0 + c + i;
+                    v[i] = (key > qrow || key >= S) ? 0.f : exp2f(v[i] * args.scale_log2 - m);
+                    psum += v[i];
+                }
+                // 32 keys = 4 chunks of 16 bytes in atom c / 64, chunk index (c % 64) / 8 + q
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int chunk = ((c & 63) >> 3) + q;
+                    uint8_t* dst = prow + (c >> 6) * ATOM + ((chunk ^ (r & 7)) << 4);
+                    uint4 pk;
+                    __nv_bfloat162 b0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+                    __nv_bfloat162 b1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+                    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+                    __nv_bfloat162 b3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+                    pk.x = *reinterpret_cast<uint32_t*>(&b0);
+                    pk.y = *reinterpret_cast<uint32_t*>(&b1);
+                    pk.z = *reinterpret_cast<uint32_t*>(&b2);
+                    pk.w = *reinterpret_cast<uint32_t*>(&b3);
+                    *reinterpret_cast<uint4*>(dst) = pk;
+                }
+            }
+            l = l * corr + psum;
+            corr_prev = corr;
+            // P visible to the tensor core (async proxy); S buffer free for S_{j+2}
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(p_full);
+                mbar_arrive(&s_free[st]);
+            }
+        }
+        if (ok && fa_wait(o_full, (nt - 1) & 1, lim)) {
+            tc_fence_after();
+            const float inv = 1.f / l;
+            __nv_bfloat16* out = args.O + ((size_t)b * S + qrow) * 2048 + h * HD;
+#pragma unroll
+            for (int c = 0; c < HD; c += 32) {
+                float v[32];
+                tmem_ld32(tmem + lane_off + 256 + c, v);
+                if (qrow < S) {
+#pragma unroll
+                    for (int i = 0; i < 32; i += 8) {
+                        uint4 pk;
+                        __nv_bfloat162 b0 = __floats2bfloat162_rn((o[c + i] * corr_prev + v[i]) * inv,
+                                                                  (o[c + i + 1] * corr_prev + v[i + 1]) * inv);
+                        __nv_bfloat162 b1 = __floats2bfloat162_rn((o[c + i + 2] * corr_prev + v[i + 2]) * inv,
+                                                                  (o[c + i + 3] * corr_prev + v[i + 3]) * inv);
+                        __nv_bfloat162 b2 = __floats2bfloat162_rn((o[c + i + 4] * corr_prev + v[i + 4]) * inv,
+                                                                  (o[c + i + 5] * corr_prev + v[i + 5]) * inv);
+                        __nv_bfloat162 b3 = __floats2bfloat162_rn((o[c + i + 6] * corr_prev + v[i + 6]) * inv,
+                                                                  (o[c + i + 7] * corr_prev + v[i + 7]) * inv);
+                        pk.x = *reinterpret_cast<uint32_t*>(&b0);
+                        pk.y = *reinterpret_cast<uint32_t*>(&b1);
+                        pk.z = *reinterpret_cast<uint32_t*>(&b2);
+                        pk.w = *reinterpret_cast<uint32_t*>(&b3);
+                        *reinterpret_cast<uint4*>(out + c + i) = pk;
+                    }
+                }
+            }
+        } else {
+            if (lane == 0) atomicExch(args.err, 43);
+            *abort_flag = 1;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+}  // namespace fa
+}  // namespace mq

@@ -48,6 +48,8 @@ struct QkvPrefillEpi {
     __nv_bfloat16* v_cache;
     long long cache_seq_stride;       // elements between sequences' caches
     int S, start_pos, max_seq;
+    __nv_bfloat16* Vt;                // optional: V transposed per (sequence, kv head): [B * 8 * 128, ldvt]
+    int ldvt;
 };
 
 struct PArgs {
@@ -90,6 +92,9 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
                                     : (map == 1 ? e.k_cache : e.v_cache) + b * e.cache_seq_stride +
                                           ((size_t)head * e.max_seq + p) * 128;
     if (map == 2) {
+        // V^T row d of (sequence b, kv head): lanes hold consecutive positions, so each
+        // scalar store of the warp covers 64 contiguous bytes
+        __nv_bfloat16* vt = e.Vt ? e.Vt + ((size_t)(b * 8 + head) * 128) * e.ldvt + (row - b * e.S) : nullptr;
 #pragma unroll 1
         for (int c = 0; c < 128; c += 32) {
             float v[32];
@@ -100,6 +105,10 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
                     const uint4 pk = pack8_bf16(v + i);
                     *reinterpret_cast<uint4*>(dst + c + i) = pk;
                     *reinterpret_cast<uint4*>(cache + c + i) = pk;
+                }
+                if (vt) {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) vt[(size_t)(c + i) * e.ldvt] = __float2bfloat16(v[i]);
                 }
             }
         }

@@ -133,12 +133,13 @@ extern "C" int mq_gemm_bf16(const void* A, int lda, const void* B, int ldb, cons
 // =============================================================================
 #include "prefill_kernels.cuh"
 #include "attn_fa.cuh"
+#include "attn_tc.cuh"
 
 namespace mq {
 namespace {
 
 struct PrefillLayout {
-    size_t X, Xn, Qb, Kb, Vb, Ob, act, lastn, logits, err, total;
+    size_t X, Xn, Qb, Kb, Vb, Vt, Ob, act, lastn, logits, err, total;
 };
 
 PrefillLayout prefill_layout(int B, int S) {
@@ -151,6 +152,7 @@ PrefillLayout prefill_layout(int B, int S) {
     L.Qb = take(M * 2048 * 2);
     L.Kb = take(M * 1024 * 2);
     L.Vb = take(M * 1024 * 2);
+    L.Vt = take((size_t)B * 8 * 128 * ((S + 7) / 8 * 8) * 2);   // V^T per (sequence, kv head), rows padded to 8
     L.Ob = take(M * 2048 * 2);
     L.act = take(M * 3072 * 2);
     L.lastn = take((size_t)B * 1024 * 2);
@@ -196,12 +198,20 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
         int dev = 0;
         if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return MQ_ERR_CUDA;
         if (!fa_configured[dev]) {
-            if (cudaFuncSetAttribute(pf::flash_attn_causal_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     pf::FA_SMEM) != cudaSuccess)
+            if (cudaFuncSetAttribute(fa::fa_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM) !=
+                cudaSuccess)
                 return MQ_ERR_CUDA;
             fa_configured[dev] = true;
         }
     }
+    // attention operands: Q [M, 2048], K [M, 1024] and V^T [B * 8 * 128, ldvt] (zero padding past S)
+    pf::bf16* Vt = (pf::bf16*)(ws + L.Vt);
+    const int ldvt = (S + 7) / 8 * 8;
+    CUtensorMap tmQ, tmK, tmV;
+    if (!make_tmap(&tmQ, Qb, (uint64_t)M, 2048, 2048, fa::BQ) || !make_tmap(&tmK, Kb, (uint64_t)M, 1024, 1024, fa::BK) ||
+        !make_tmap(&tmV, Vt, (uint64_t)B * 8 * 128, (uint64_t)ldvt, (uint64_t)ldvt, 128))
+        return MQ_ERR_CUDA;
+    if (ldvt != S && cudaMemsetAsync(Vt, 0, (size_t)B * 8 * 128 * ldvt * 2, st) != cudaSuccess) return MQ_ERR_CUDA;
     pf::embed_kernel<<<(M + 7) / 8, 256, 0, st>>>(p->ids, (const pf::bf16*)p->embed, X, M);
     for (int l = 0; l < p->num_layers; ++l) {
         const LDGLayerWeights& W = p->layers_host[l];
@@ -223,12 +233,22 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             e.S = S;
             e.start_pos = 0;
             e.max_seq = p->max_seq_len;
+            e.Vt = Vt;
+            e.ldvt = ldvt;
             const void* Bm[3] = {W.q_proj_weight, W.k_proj_weight, W.v_proj_weight};
             const int Nm[3] = {2048, 1024, 1024};
             MQ_TRY(launch_persist<EPI_QKV>(Xn, 1024, Bm, Nm, 3, 1024, nullptr, 0, M, 1024, &e, err, st));
         }
-        dim3 fgrid((S + pf::FA_B - 1) / pf::FA_B, MQ_NUM_Q_HEADS, B);
-        pf::flash_attn_causal_kernel<<<fgrid, 128, pf::FA_SMEM, st>>>(Qb, Kb, Vb, Ob, S, scale_log2);
+        {
+            fa::Args fa_args;
+            fa_args.O = Ob;
+            fa_args.S = S;
+            fa_args.scale_log2 = scale_log2;
+            fa_args.err = err;
+            fa_args.timeout_cycles = 4000000000ll;
+            dim3 fgrid((S + fa::BQ - 1) / fa::BQ, MQ_NUM_Q_HEADS, B);
+            fa::fa_tc_kernel<<<fgrid, fa::THREADS, fa::SMEM, st>>>(tmQ, tmK, tmV, fa_args);
+        }
         MQ_TRY(gemm_bf16(Ob, 2048, W.o_proj_weight, 2048, nullptr, X, 1024, M, 1024, 2048, EPI_ADD_F32, err, st));
         pf::rmsnorm_bf16_kernel<<<(M + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)W.post_attn_layernorm_weight, Xn, M,
                                                                1, 0);
