@@ -1,7 +1,7 @@
 // Causal GQA flash attention for prefill on the 5th-generation tensor cores
 // (tcgen05, accumulators in TMEM).
 //
-// One CTA = (block of 128 query rows, q head, sequence); 192 threads:
+// One CTA = (block of 128 query rows, q head, sequence); 320 threads:
 //   warp 0      TMA producer: Q once, then K and V^T tiles of 128 keys into a
 //               2-stage ring;
 //   warp 1      TMEM owner; one thread issues the MMAs:
@@ -11,11 +11,14 @@
 //                                 the O buffer;
 //               S_{j+1} is issued before O_j so the tensor core works while
 //               the softmax warps are busy;
-//   warps 2-5   softmax and output, one query row per thread (TMEM lane):
-//               row max and exp2 of S_j in registers, P_j written as bf16 to
-//               shared memory in the 128-byte-swizzled K-major layout the MMA
-//               reads, and O_{j-1} folded into a register accumulator with
-//               the online-softmax correction.
+//   warps 2-9   softmax and output: warp w owns query rows 32 (w % 4) ..
+//               (its TMEM lane quadrant) and column half (w - 2) / 4 of S
+//               and O; row maxima are exchanged with the partner warp through
+//               shared memory.  exp2 of S_j in registers, P_j written as bf16
+//               to shared memory in the 128-byte-swizzled K-major layout the
+//               MMA reads, and O_{j-1} folded into a register accumulator with
+//               the online-softmax correction; each half keeps its own row
+//               sum, added at the end.
 // All operands are K-major: Q [q][d], K [key][d], P [q][key] and V^T [d][key]
 // (the QKV GEMM epilogue writes V transposed per sequence and kv head).
 // Scores are in the log2 domain.  Every wait is bounded and sets an error code.
@@ -38,8 +41,10 @@ constexpr int SM_K = SM_Q + TILE;           // [2] stages
 constexpr int SM_V = SM_K + 2 * TILE;       // [2] stages (V^T)
 constexpr int SM_P = SM_V + 2 * TILE;
 constexpr int SM_BAR = SM_P + TILE;
-constexpr int SMEM = SM_BAR + 256 + 1024;   // + barriers + alignment slack
-constexpr int THREADS = 192;
+constexpr int SM_RED = SM_BAR + 128;        // fp32 [2 tiles][2 halves][128 rows] row maxima
+constexpr int SMEM = SM_RED + 2 * 2 * 128 * 4 + 1024;   // + barriers, row-max exchange, alignment slack
+constexpr int SOFT_WARPS = 8;               // two warps per TMEM lane quadrant, one per column half
+constexpr int THREADS = 64 + 32 * SOFT_WARPS;
 
 struct Args {
     __nv_bfloat16* O;       // [M, 2048] bf16, row m = b * S + s
@@ -48,6 +53,13 @@ struct Args {
     int* err;
     long long timeout_cycles;
 };
+
+// 2^x on the special-function unit (ex2.approx.ftz: 2^-inf = 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
 __device__ __forceinline__ bool fa_wait(uint64_t* bar, uint32_t parity, long long limit) {
     const long long t0 = clock64();
@@ -90,11 +102,11 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             mbar_init(&kv_full[i], 1);
             mbar_init(&kv_empty[i], 1);
             mbar_init(&s_full[i], 1);
-            mbar_init(&s_free[i], 4);
+            mbar_init(&s_free[i], SOFT_WARPS);
         }
-        mbar_init(p_full, 4);
+        mbar_init(p_full, SOFT_WARPS);
         mbar_init(o_full, 1);
-        mbar_init(o_free, 4);
+        mbar_init(o_free, SOFT_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmQ);
@@ -182,47 +194,51 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             }
         }
     } else {
-        // softmax / output: thread = query row r of the block (TMEM lane r)
-        const int quad = warp & 3;
+        // softmax / output: thread = (query row r, column half hh)
+        const int quad = warp & 3, hh = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int qrow = q0 + r;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-        float o[HD];
+        float* red = reinterpret_cast<float*>(smem + SM_RED);     // [2][2][128]
+        float o[HD / 2];
 #pragma unroll
-        for (int i = 0; i < HD; ++i) o[i] = 0.f;
+        for (int i = 0; i < HD / 2; ++i) o[i] = 0.f;
         float m = -INFINITY, l = 0.f, corr_prev = 1.f;
-        uint8_t* prow = smem + SM_P + r * 128;
+        uint8_t* prow = smem + SM_P + hh * ATOM + r * 128;    // keys 64 hh .. 64 hh + 63 = one swizzled atom
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
             const int st = j & 1, u = j >> 1;
             if (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag) { ok = false; break; }
             tc_fence_after();
-            const uint32_t sa = tmem + lane_off + st * BK;
-            const int k0 = j * BK;
-            // pass 1: row max of the tile (scaled, causal and length masked)
+            const int k0 = j * BK + hh * 64;
+            const uint32_t sa = tmem + lane_off + st * BK + hh * 64;
+            // pass 1: this half's row max (scaled, causal and length masked)
             float tmax = -INFINITY;
 #pragma unroll 1
-            for (int c = 0; c < BK; c += 32) {
+            for (int c = 0; c < 64; c += 32) {
                 float v[32];
                 tmem_ld32(sa + c, v);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int key = k0 + c + i;
-                    const float x = (key > qrow || key >= S) ? -INFINITY : v[i] * args.scale_log2;
-                    tmax = fmaxf(tmax, x);
+                    tmax = fmaxf(tmax, (key > qrow || key >= S) ? -INFINITY : v[i] * args.scale_log2);
                 }
             }
+            // row maximum over both halves (partner warp w +- 4 shares the lane quadrant)
+            red[(st * 2 + hh) * 128 + r] = tmax;
+            named_bar_sync(1 + quad, 64);
+            tmax = fmaxf(tmax, red[(st * 2 + (hh ^ 1)) * 128 + r]);
             const float mn = fmaxf(m, tmax);
-            const float corr = exp2f(m - mn);   // 0 on the first tile (m = -inf)
+            const float corr = ex2_approx(m - mn);   // 0 on the first tile (m = -inf)
             m = mn;
             // fold O_{j-1} (relative to the previous max) before P_j overwrites P_{j-1}
             if (j >= 1) {
                 if (!fa_wait(o_full, (j - 1) & 1, lim)) { ok = false; break; }
                 tc_fence_after();
 #pragma unroll
-                for (int c = 0; c < HD; c += 32) {
+                for (int c = 0; c < HD / 2; c += 32) {
                     float v[32];
-                    tmem_ld32(tmem + lane_off + 256 + c, v);
+                    tmem_ld32(tmem + lane_off + 256 + hh * 64 + c, v);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * corr_prev + v[i];
                 }
@@ -230,23 +246,21 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                 __syncwarp();
                 if (lane == 0) mbar_arrive(o_free);
             }
-            // pass 2: P = exp2(s - m) as bf16 into the swizzled P tile, row sum
+            // pass 2: P = exp2(s - m) as bf16 into this half's swizzled atom; this half's row sum
             float psum = 0.f;
 #pragma unroll 1
-            for (int c = 0; c < BK; c += 32) {
+            for (int c = 0; c < 64; c += 32) {
                 float v[32];
                 tmem_ld32(sa + c, v);
 #pragma unroll
                 for (int i = 0; i < 32; ++i) {
                     const int key = k0 + c + i;
-                    v[i] = (key > qrow || key >= S) ? 0.f : exp2f(v[i] * args.scale_log2 - m);
+                    v[i] = (key > qrow || key >= S) ? 0.f : ex2_approx(v[i] * args.scale_log2 - m);
                     psum += v[i];
                 }
-                // 32 keys = 4 chunks of 16 bytes in atom c / 64, chunk index (c % 64) / 8 + q
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
-                    const int chunk = ((c & 63) >> 3) + q;
-                    uint8_t* dst = prow + (c >> 6) * ATOM + ((chunk ^ (r & 7)) << 4);
+                    const int ch = (c >> 3) + q;
                     uint4 pk;
                     __nv_bfloat162 b0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
                     __nv_bfloat162 b1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
@@ -256,7 +270,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                     pk.y = *reinterpret_cast<uint32_t*>(&b1);
                     pk.z = *reinterpret_cast<uint32_t*>(&b2);
                     pk.w = *reinterpret_cast<uint32_t*>(&b3);
-                    *reinterpret_cast<uint4*>(dst) = pk;
+                    *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
                 }
             }
             l = l * corr + psum;
@@ -270,26 +284,29 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                 mbar_arrive(&s_free[st]);
             }
         }
+        // both halves' row sums (same running max)
+        named_bar_sync(1 + quad, 64);
+        red[hh * 128 + r] = l;
+        named_bar_sync(1 + quad, 64);
+        const float ltot = l + red[(hh ^ 1) * 128 + r];
         if (ok && fa_wait(o_full, (nt - 1) & 1, lim)) {
             tc_fence_after();
-            const float inv = 1.f / l;
-            __nv_bfloat16* out = args.O + ((size_t)b * S + qrow) * 2048 + h * HD;
+            const float inv = 1.f / ltot;
+            __nv_bfloat16* out = args.O + ((size_t)b * S + qrow) * 2048 + h * HD + hh * 64;
 #pragma unroll
-            for (int c = 0; c < HD; c += 32) {
+            for (int c = 0; c < HD / 2; c += 32) {
                 float v[32];
-                tmem_ld32(tmem + lane_off + 256 + c, v);
+                tmem_ld32(tmem + lane_off + 256 + hh * 64 + c, v);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = (o[c + i] * corr_prev + v[i]) * inv;
                 if (qrow < S) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
                         uint4 pk;
-                        __nv_bfloat162 b0 = __floats2bfloat162_rn((o[c + i] * corr_prev + v[i]) * inv,
-                                                                  (o[c + i + 1] * corr_prev + v[i + 1]) * inv);
-                        __nv_bfloat162 b1 = __floats2bfloat162_rn((o[c + i + 2] * corr_prev + v[i + 2]) * inv,
-                                                                  (o[c + i + 3] * corr_prev + v[i + 3]) * inv);
-                        __nv_bfloat162 b2 = __floats2bfloat162_rn((o[c + i + 4] * corr_prev + v[i + 4]) * inv,
-                                                                  (o[c + i + 5] * corr_prev + v[i + 5]) * inv);
-                        __nv_bfloat162 b3 = __floats2bfloat162_rn((o[c + i + 6] * corr_prev + v[i + 6]) * inv,
-                                                                  (o[c + i + 7] * corr_prev + v[i + 7]) * inv);
+                        __nv_bfloat162 b0 = __floats2bfloat162_rn(v[i], v[i + 1]);
+                        __nv_bfloat162 b1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+                        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+                        __nv_bfloat162 b3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
                         pk.x = *reinterpret_cast<uint32_t*>(&b0);
                         pk.y = *reinterpret_cast<uint32_t*>(&b1);
                         pk.z = *reinterpret_cast<uint32_t*>(&b2);
