@@ -7,8 +7,8 @@
 //   warp 1      TMEM owner; one thread issues the MMAs:
 //                 S_j = Q K_j^T  (M=128 queries, N=128 keys, K=128 dims) into
 //                                 one of two S buffers,
-//                 O_j = P_j V_j  (M=128 queries, N=128 dims, K=128 keys) into
-//                                 the O buffer;
+//                 O += P_j V_j   (M=128 queries, N=128 dims, K=128 keys),
+//                                 accumulated in TMEM across the key tiles;
 //               S_{j+1} is issued before O_j so the tensor core works while
 //               the softmax warps are busy;
 //   warps 2-9   softmax and output: warp w owns query rows 32 (w % 4) ..
@@ -16,9 +16,11 @@
 //               and O; row maxima are exchanged with the partner warp through
 //               shared memory.  exp2 of S_j in registers, P_j written as bf16
 //               to shared memory in the 128-byte-swizzled K-major layout the
-//               MMA reads, and O_{j-1} folded into a register accumulator with
-//               the online-softmax correction; each half keeps its own row
-//               sum, added at the end.
+//               MMA reads.  P is taken relative to the row maximum in use; O
+//               in TMEM is rescaled (tcgen05.ld / st) only when a row maximum
+//               grows by more than 2^8, so P stays below 256 and most tiles
+//               touch O not at all.  Each half keeps its own row sum, added at
+//               the end.
 // All operands are K-major: Q [q][d], K [key][d], P [q][key] and V^T [d][key]
 // (the QKV GEMM epilogue writes V transposed per sequence and kv head).
 // Scores are in the log2 domain.  Every wait is bounded and sets an error code.
@@ -83,7 +85,6 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     uint64_t* s_free = bars + 7;      // [2]
     uint64_t* p_full = bars + 9;
     uint64_t* o_full = bars + 10;
-    uint64_t* o_free = bars + 11;
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -106,7 +107,6 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
         }
         mbar_init(p_full, SOFT_WARPS);
         mbar_init(o_full, 1);
-        mbar_init(o_free, SOFT_WARPS);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmQ);
@@ -153,14 +153,15 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             bool ok = fa_wait(q_full, 0, lim);
             // O_j = P_j V_j into the O buffer
             auto pv = [&](int j) -> bool {
+                // P_j written and O rescaled (if the row maxima moved) by the softmax warps
                 if (!fa_wait(p_full, j & 1, lim)) return false;
-                if (j >= 1 && !fa_wait(o_free, (j - 1) & 1, lim)) return false;
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + SM_V + (j & 1) * TILE);
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k) {
                     const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
-                    tc_mma_f16(tmem + 256, sw128_kmajor_desc(sp + off), sw128_kmajor_desc(sv + off), idesc, k != 0);
+                    tc_mma_f16(tmem + 256, sw128_kmajor_desc(sp + off), sw128_kmajor_desc(sv + off), idesc,
+                               (j | k) != 0);
                 }
                 tc_commit(o_full);
                 tc_commit(&kv_empty[j & 1]);
@@ -199,92 +200,88 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
         const int r = quad * 32 + lane;
         const int qrow = q0 + r;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+        const uint32_t oa = tmem + lane_off + 256 + hh * 64;   // this thread's half of its O row
         float* red = reinterpret_cast<float*>(smem + SM_RED);     // [2][2][128]
-        float o[HD / 2];
-#pragma unroll
-        for (int i = 0; i < HD / 2; ++i) o[i] = 0.f;
-        float m = -INFINITY, l = 0.f, corr_prev = 1.f;
+        constexpr float RESCALE_LOG2 = 8.f;
+        float m = -INFINITY, l = 0.f;
         uint8_t* prow = smem + SM_P + hh * ATOM + r * 128;    // keys 64 hh .. 64 hh + 63 = one swizzled atom
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
             const int st = j & 1, u = j >> 1;
-            if (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag) { ok = false; break; }
+            // after a failed wait the loop still runs to the end (without waiting) so that the
+            // partner warp's named barriers are always matched
+            if (ok && (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag)) ok = false;
             tc_fence_after();
             const int k0 = j * BK + hh * 64;
-            const uint32_t sa = tmem + lane_off + st * BK + hh * 64;
-            // pass 1: this half's row max (scaled, causal and length masked)
+            float sv[64];
+            tmem_ld32(tmem + lane_off + st * BK + hh * 64, sv);
+            tmem_ld32(tmem + lane_off + st * BK + hh * 64 + 32, sv + 32);
+            // S buffer consumed: the MMA may compute S_{j+2} into it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&s_free[st]);
             float tmax = -INFINITY;
-#pragma unroll 1
-            for (int c = 0; c < 64; c += 32) {
-                float v[32];
-                tmem_ld32(sa + c, v);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int key = k0 + c + i;
-                    tmax = fmaxf(tmax, (key > qrow || key >= S) ? -INFINITY : v[i] * args.scale_log2);
-                }
+            for (int i = 0; i < 64; ++i) {
+                const int key = k0 + i;
+                sv[i] = (key > qrow || key >= S) ? -INFINITY : sv[i] * args.scale_log2;
+                tmax = fmaxf(tmax, sv[i]);
             }
             // row maximum over both halves (partner warp w +- 4 shares the lane quadrant)
             red[(st * 2 + hh) * 128 + r] = tmax;
             named_bar_sync(1 + quad, 64);
             tmax = fmaxf(tmax, red[(st * 2 + (hh ^ 1)) * 128 + r]);
-            const float mn = fmaxf(m, tmax);
-            const float corr = ex2_approx(m - mn);   // 0 on the first tile (m = -inf)
-            m = mn;
-            // fold O_{j-1} (relative to the previous max) before P_j overwrites P_{j-1}
+            // PV_{j-1} has completed: P may be overwritten and O is stable
             if (j >= 1) {
-                if (!fa_wait(o_full, (j - 1) & 1, lim)) { ok = false; break; }
+                if (ok && !fa_wait(o_full, (j - 1) & 1, lim)) ok = false;
                 tc_fence_after();
+            }
+            // move the row to a new maximum only when it grew by more than 2^8
+            float corr = 1.f;
+            if (tmax > m + RESCALE_LOG2) {
+                corr = ex2_approx(m - tmax);   // 0 on the first tile (m = -inf)
+                m = tmax;
+            }
+            l *= corr;
+            if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
 #pragma unroll
-                for (int c = 0; c < HD / 2; c += 32) {
+                for (int c = 0; c < 64; c += 32) {
                     float v[32];
-                    tmem_ld32(tmem + lane_off + 256 + hh * 64 + c, v);
+                    tmem_ld32(oa + c, v);
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[c + i] = o[c + i] * corr_prev + v[i];
+                    for (int i = 0; i < 32; ++i) v[i] *= corr;
+                    tmem_st32(oa + c, v);
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(o_free);
             }
-            // pass 2: P = exp2(s - m) as bf16 into this half's swizzled atom; this half's row sum
+            // P = exp2(s - m) (at most 2^8) as bf16 into this half's swizzled atom; row sum
             float psum = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < 64; c += 32) {
-                float v[32];
-                tmem_ld32(sa + c, v);
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int key = k0 + c + i;
-                    v[i] = (key > qrow || key >= S) ? 0.f : ex2_approx(v[i] * args.scale_log2 - m);
-                    psum += v[i];
-                }
+            for (int ch = 0; ch < 8; ++ch) {
+                float pv[8];
 #pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int ch = (c >> 3) + q;
-                    uint4 pk;
-                    __nv_bfloat162 b0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
-                    __nv_bfloat162 b1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
-                    __nv_bfloat162 b2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
-                    __nv_bfloat162 b3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
-                    pk.x = *reinterpret_cast<uint32_t*>(&b0);
-                    pk.y = *reinterpret_cast<uint32_t*>(&b1);
-                    pk.z = *reinterpret_cast<uint32_t*>(&b2);
-                    pk.w = *reinterpret_cast<uint32_t*>(&b3);
-                    *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
+                for (int q = 0; q < 8; ++q) {
+                    pv[q] = ex2_approx(sv[8 * ch + q] - m);
+                    psum += pv[q];
                 }
+                uint4 pk;
+                __nv_bfloat162 b0 = __floats2bfloat162_rn(pv[0], pv[1]);
+                __nv_bfloat162 b1 = __floats2bfloat162_rn(pv[2], pv[3]);
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(pv[4], pv[5]);
+                __nv_bfloat162 b3 = __floats2bfloat162_rn(pv[6], pv[7]);
+                pk.x = *reinterpret_cast<uint32_t*>(&b0);
+                pk.y = *reinterpret_cast<uint32_t*>(&b1);
+                pk.z = *reinterpret_cast<uint32_t*>(&b2);
+                pk.w = *reinterpret_cast<uint32_t*>(&b3);
+                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
             }
-            l = l * corr + psum;
-            corr_prev = corr;
-            // P visible to the tensor core (async proxy); S buffer free for S_{j+2}
+            l += psum;
+            // P visible to the tensor core (async proxy), O rescale done: PV_j may start
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(p_full);
-                mbar_arrive(&s_free[st]);
-            }
+            if (lane == 0) mbar_arrive(p_full);
         }
-        // both halves' row sums (same running max)
+        // both halves' row sums (same row maximum)
         named_bar_sync(1 + quad, 64);
         red[hh * 128 + r] = l;
         named_bar_sync(1 + quad, 64);
@@ -294,19 +291,17 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             const float inv = 1.f / ltot;
             __nv_bfloat16* out = args.O + ((size_t)b * S + qrow) * 2048 + h * HD + hh * 64;
 #pragma unroll
-            for (int c = 0; c < HD / 2; c += 32) {
+            for (int c = 0; c < 64; c += 32) {
                 float v[32];
-                tmem_ld32(tmem + lane_off + 256 + hh * 64 + c, v);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = (o[c + i] * corr_prev + v[i]) * inv;
+                tmem_ld32(oa + c, v);
                 if (qrow < S) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
                         uint4 pk;
-                        __nv_bfloat162 b0 = __floats2bfloat162_rn(v[i], v[i + 1]);
-                        __nv_bfloat162 b1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
-                        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
-                        __nv_bfloat162 b3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+                        __nv_bfloat162 b0 = __floats2bfloat162_rn(v[i] * inv, v[i + 1] * inv);
+                        __nv_bfloat162 b1 = __floats2bfloat162_rn(v[i + 2] * inv, v[i + 3] * inv);
+                        __nv_bfloat162 b2 = __floats2bfloat162_rn(v[i + 4] * inv, v[i + 5] * inv);
+                        __nv_bfloat162 b3 = __floats2bfloat162_rn(v[i + 6] * inv, v[i + 7] * inv);
                         pk.x = *reinterpret_cast<uint32_t*>(&b0);
                         pk.y = *reinterpret_cast<uint32_t*>(&b1);
                         pk.z = *reinterpret_cast<uint32_t*>(&b2);
