@@ -1,7 +1,8 @@
 // Persistent tcgen05 GEMM for prefill: C[M, N] = A[M, K] . B[N, K]^T, bf16
 // operands (both K-major), fp32 accumulation in TMEM, fused epilogues.
 //
-// One CTA per SM walks the 128 x 128 output tiles t = blockIdx.x, + gridDim.x ..
+// One CTA per SM walks the 128 x BN output tiles t = blockIdx.x, + gridDim.x ..
+// (BN = 256 where every B map allows it: half the A re-reads per FLOP)
 // Warp 0 (one thread) streams A/B K-slices of 64 through an mbarrier ring with
 // TMA; warp 1 owns TMEM and one of its threads issues the MMAs; warps 2-5 run
 // the epilogue.  The accumulator is double-buffered in TMEM, so the epilogue
@@ -12,7 +13,7 @@
 // [0, nb0) read map 0, [nb0, nb0 + nb1) map 1, the rest map 2.  EPI_SILU_MUL
 // reads gate (map 0) and up (map 1) for the same tile into two accumulators.
 //
-// EPI_QKV (prefill QKV projection): one 128-column tile is one head.  q and k
+// EPI_QKV (prefill QKV projection): each 128 columns of a tile are one head.  q and k
 // heads get RMSNorm over the head (x norm weight) and rotate-half RoPE at the
 // row's position, in the thread that owns the row (no cross-thread traffic);
 // q goes to Qb, k and v to Kb / Vb and to the sequence's K/V cache (bf16).
@@ -26,14 +27,16 @@ namespace mq {
 
 constexpr int EPI_QKV = 4;
 
-template <int EPI>
+template <int EPI, int BN>
 struct PCfg {
     static constexpr int NB = (EPI == EPI_SILU_MUL) ? 2 : 1;          // B tiles per stage
-    static constexpr int STAGE = GEMM_TILE_BYTES * (1 + NB);
-    static constexpr int NSTAGES = (EPI == EPI_SILU_MUL) ? 4 : 6;
-    static constexpr int ACC_COLS = GEMM_BN * NB;                     // one accumulator buffer
+    static constexpr int B_BYTES = BN * GEMM_BK * 2;                  // one B tile (BN rows x 64)
+    static constexpr int STAGE = GEMM_TILE_BYTES + NB * B_BYTES;      // A tile (128 rows) + B tiles
+    static constexpr int NSTAGES = (6 * STAGE <= 200 * 1024) ? 6 : 4;
+    static constexpr int ACC_COLS = BN * NB;                          // one accumulator buffer
     static constexpr int TMEM_COLS = 2 * ACC_COLS;                    // double-buffered
     static constexpr int SMEM = NSTAGES * STAGE + 1024 + 256;
+    static_assert(TMEM_COLS <= 512, "two accumulator buffers fit in TMEM");
 };
 
 struct QkvPrefillEpi {
@@ -170,12 +173,12 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
     }
 }
 
-template <int EPI>
+template <int EPI, int BN>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
 gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
                     const PArgs args) {
-    using Cfg = PCfg<EPI>;
+    using Cfg = PCfg<EPI, BN>;
     extern __shared__ uint8_t persist_smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(persist_smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::NSTAGES * Cfg::STAGE);
@@ -229,7 +232,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         tb = &tmB2;
                     }
                 }
-                const int n0 = nt * GEMM_BN;
+                const int n0 = nt * BN;
                 for (int kb = 0; kb < nk; ++kb, ++g) {
                     const uint32_t s = g % Cfg::NSTAGES;
                     if (g >= (uint32_t)Cfg::NSTAGES &&
@@ -242,7 +245,8 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     mbar_arrive_expect_tx(&full[s], Cfg::STAGE);
                     tma_load_2d(st, &tmA, kb * GEMM_BK, m0, &full[s]);
                     tma_load_2d(st + GEMM_TILE_BYTES, tb, kb * GEMM_BK, n0, &full[s]);
-                    if (Cfg::NB == 2) tma_load_2d(st + 2 * GEMM_TILE_BYTES, &tmB1, kb * GEMM_BK, n0, &full[s]);
+                    if (Cfg::NB == 2)
+                        tma_load_2d(st + GEMM_TILE_BYTES + Cfg::B_BYTES, &tmB1, kb * GEMM_BK, n0, &full[s]);
                 }
             }
             // on an abort every copy still in flight lands before the CTA may exit
@@ -252,7 +256,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, GEMM_BN);
+            constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN);
             uint32_t g = 0;
             int i = 0;
             for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++i) {
@@ -278,8 +282,8 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         const uint64_t ad = sw128_kmajor_desc(sa + k * 32);
                         tc_mma_f16(acc, ad, sw128_kmajor_desc(sa + GEMM_TILE_BYTES + k * 32), idesc, (kb | k) != 0);
                         if (Cfg::NB == 2)
-                            tc_mma_f16(acc + GEMM_BN, ad, sw128_kmajor_desc(sa + 2 * GEMM_TILE_BYTES + k * 32), idesc,
-                                       (kb | k) != 0);
+                            tc_mma_f16(acc + BN, ad, sw128_kmajor_desc(sa + GEMM_TILE_BYTES + Cfg::B_BYTES + k * 32),
+                                       idesc, (kb | k) != 0);
                     }
                     tc_commit(&empty[s]);
                 }
@@ -312,15 +316,17 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         map = 2;
                     }
                 }
-                qkv_row_epilogue(args, acc, map, head, row);
+#pragma unroll 1
+                for (int hd = 0; hd < BN / 128; ++hd)
+                    qkv_row_epilogue(args, acc + hd * 128, map, head * (BN / 128) + hd, row);
             } else {
-                const int n0 = nt_all * GEMM_BN;
-                for (int c = 0; c < GEMM_BN; c += 32) {
+                const int n0 = nt_all * BN;
+                for (int c = 0; c < BN; c += 32) {
                     float v[32];
                     tmem_ld32(acc + c, v);
                     if (EPI == EPI_SILU_MUL) {
                         float up[32];
-                        tmem_ld32(acc + GEMM_BN + c, up);
+                        tmem_ld32(acc + BN + c, up);
 #pragma unroll
                         for (int q = 0; q < 32; ++q) v[q] = v[q] / (1.0f + expf(-v[q])) * up[q];
                     }

@@ -56,17 +56,17 @@ int num_sms() {
 }
 
 // One persistent GEMM launch: A [M, K] against up to three B maps side by side
-// (Nmap[i] rows each; EPI_SILU_MUL: gate, up), one CTA per SM.
-template <int EPI>
-int launch_persist(const void* A, int lda, const void* const* Bm, const int* Nmap, int nmaps, int ldb, void* C, int ldc,
-                   int M, int K, const QkvPrefillEpi* qkv, int* err, cudaStream_t stream) {
-    using Cfg = PCfg<EPI>;
+// (Nmap[i] rows each; EPI_SILU_MUL: gate, up), one CTA per SM, BN-wide tiles.
+template <int EPI, int BN>
+int launch_persist_bn(const void* A, int lda, const void* const* Bm, const int* Nmap, int nmaps, int ldb, void* C,
+                      int ldc, int M, int K, const QkvPrefillEpi* qkv, int* err, cudaStream_t stream) {
+    using Cfg = PCfg<EPI, BN>;
     static bool configured[64] = {false};
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return MQ_ERR_CUDA;
     if (dev < 64 && !configured[dev]) {
-        if (cudaFuncSetAttribute(gemm_persist_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(gemm_persist_kernel<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 Cfg::SMEM) != cudaSuccess)
             return MQ_ERR_CUDA;
         configured[dev] = true;
     }
@@ -74,7 +74,7 @@ int launch_persist(const void* A, int lda, const void* const* Bm, const int* Nma
     if (!make_tmap(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, GEMM_BM)) return MQ_ERR_CUDA;
     for (int i = 0; i < 3; ++i) {
         const int m = i < nmaps ? i : nmaps - 1;
-        if (!make_tmap(&tb[i], Bm[m], (uint64_t)Nmap[m], (uint64_t)K, (uint64_t)ldb, GEMM_BN)) return MQ_ERR_CUDA;
+        if (!make_tmap(&tb[i], Bm[m], (uint64_t)Nmap[m], (uint64_t)K, (uint64_t)ldb, BN)) return MQ_ERR_CUDA;
     }
     PArgs a = {};
     a.C = C;
@@ -82,16 +82,34 @@ int launch_persist(const void* A, int lda, const void* const* Bm, const int* Nma
     a.M = M;
     a.K = K;
     a.tiles_m = (M + GEMM_BM - 1) / GEMM_BM;
-    a.nb0 = Nmap[0] / GEMM_BN;
-    a.nb1 = nmaps > 1 ? Nmap[1] / GEMM_BN : 0;
-    a.tiles_n = EPI == EPI_SILU_MUL ? a.nb0 : a.nb0 + a.nb1 + (nmaps > 2 ? Nmap[2] / GEMM_BN : 0);
+    a.nb0 = Nmap[0] / BN;
+    a.nb1 = nmaps > 1 ? Nmap[1] / BN : 0;
+    a.tiles_n = EPI == EPI_SILU_MUL ? a.nb0 : a.nb0 + a.nb1 + (nmaps > 2 ? Nmap[2] / BN : 0);
     if (qkv) a.qkv = *qkv;
     a.err = err;
     a.timeout_cycles = 4000000000ll;  // ~2 s at 1.9 GHz
     const int ntiles = a.tiles_m * a.tiles_n;
     const int grid = ntiles < num_sms() ? ntiles : num_sms();
-    gemm_persist_kernel<EPI><<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb[0], tb[1], tb[2], a);
+    gemm_persist_kernel<EPI, BN><<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb[0], tb[1], tb[2], a);
     return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+}
+
+// 256-wide tiles where every B map's rows allow them (gate/up keep 128: two accumulators)
+template <int EPI>
+int launch_persist(const void* A, int lda, const void* const* Bm, const int* Nmap, int nmaps, int ldb, void* C, int ldc,
+                   int M, int K, const QkvPrefillEpi* qkv, int* err, cudaStream_t stream) {
+    bool wide = EPI != EPI_SILU_MUL;
+    int ncols = 0;
+    for (int i = 0; i < nmaps; ++i) {
+        wide = wide && Nmap[i] % 256 == 0;
+        ncols += Nmap[i];
+    }
+    // only when the wide tiles still fill every SM at least once
+    wide = wide && (long long)((M + GEMM_BM - 1) / GEMM_BM) * (ncols / 256) >= num_sms();
+    if (EPI != EPI_SILU_MUL && wide)
+        return launch_persist_bn<EPI, (EPI == EPI_SILU_MUL ? 128 : 256)>(A, lda, Bm, Nmap, nmaps, ldb, C, ldc, M, K,
+                                                                         qkv, err, stream);
+    return launch_persist_bn<EPI, 128>(A, lda, Bm, Nmap, nmaps, ldb, C, ldc, M, K, qkv, err, stream);
 }
 
 template <int EPI>
