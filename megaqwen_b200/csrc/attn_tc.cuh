@@ -14,14 +14,14 @@
 //   warps 2-9   softmax and output: warp w owns query rows 32 (w % 4) ..
 //               (its TMEM lane quadrant) and column half (w - 2) / 4 of S
 //               and O; row maxima are exchanged with the partner warp through
-//               shared memory.  exp2 of S_j in registers, P_j written as bf16
-//               to shared memory in the 128-byte-swizzled K-major layout the
-//               MMA reads.  P is taken relative to the row maximum in use; O
+//               shared memory.  exp2 of S_j in registers, P_j stored as bf16
+//               into one of two TMEM buffers, from which the P V MMA reads
+//               its A operand.  P is taken relative to the row maximum in use; O
 //               in TMEM is rescaled (tcgen05.ld / st) only when a row maximum
 //               grows by more than 2^8, so P stays below 256 and most tiles
 //               touch O not at all.  Each half keeps its own row sum, added at
 //               the end.
-// All operands are K-major: Q [q][d], K [key][d], P [q][key] and V^T [d][key]
+// All operands are K-major: Q [q][d], K [key][d], P [q][key] (TMEM) and V^T [d][key]
 // (the QKV GEMM epilogue writes V transposed per sequence and kv head).
 // Scores are in the log2 domain.  Every wait is bounded and sets an error code.
 #pragma once
@@ -41,12 +41,14 @@ constexpr int TILE = 2 * ATOM;              // a 128 x 128 bf16 operand (32 KB)
 constexpr int SM_Q = 0;
 constexpr int SM_K = SM_Q + TILE;           // [2] stages
 constexpr int SM_V = SM_K + 2 * TILE;       // [2] stages (V^T)
-constexpr int SM_P = SM_V + 2 * TILE;
-constexpr int SM_BAR = SM_P + TILE;
+constexpr int SM_BAR = SM_V + 2 * TILE;
 constexpr int SM_RED = SM_BAR + 128;        // fp32 [2 tiles][2 halves][128 rows] row maxima
 constexpr int SMEM = SM_RED + 2 * 2 * 128 * 4 + 1024;   // + barriers, row-max exchange, alignment slack
 constexpr int SOFT_WARPS = 8;               // two warps per TMEM lane quadrant, one per column half
 constexpr int THREADS = 64 + 32 * SOFT_WARPS;
+// TMEM columns: S_j buffers at 0 / 128 (fp32), O at 256 (fp32), P_j buffers at
+// 384 / 448 (bf16 packed two per column: 128 keys = 64 columns)
+constexpr uint32_t TM_O = 256, TM_P = 384;
 
 struct Args {
     __nv_bfloat16* O;       // [M, 2048] bf16, row m = b * S + s
@@ -83,9 +85,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     uint64_t* kv_empty = bars + 3;    // [2]
     uint64_t* s_full = bars + 5;      // [2]
     uint64_t* s_free = bars + 7;      // [2]
-    uint64_t* p_full = bars + 9;
-    uint64_t* o_full = bars + 10;
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 12);
+    uint64_t* p_full = bars + 9;      // [2] P_j stored on p_full[j & 1] (one barrier per P buffer)
+    uint64_t* o_full = bars + 11;     // [2] PV_j completion on o_full[j & 1]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int S = args.S;
@@ -105,8 +107,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], SOFT_WARPS);
         }
-        mbar_init(p_full, SOFT_WARPS);
-        mbar_init(o_full, 1);
+        mbar_init(&p_full[0], SOFT_WARPS);
+        mbar_init(&p_full[1], SOFT_WARPS);
+        mbar_init(&o_full[0], 1);
+        mbar_init(&o_full[1], 1);
         *abort_flag = 0;
         fence_mbar_init();
         prefetch_tmap(&tmQ);
@@ -120,7 +124,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    const uint32_t tmem = *tmem_holder;       // S buffers at columns 0 / 128, O at 256
+    const uint32_t tmem = *tmem_holder;
 
     if (warp == 0) {
         if (lane == 0) {
@@ -149,21 +153,21 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(BQ, BK);
-            const uint32_t sq = smem_u32(smem + SM_Q), sp = smem_u32(smem + SM_P);
+            const uint32_t sq = smem_u32(smem + SM_Q);
             bool ok = fa_wait(q_full, 0, lim);
             // O_j = P_j V_j into the O buffer
             auto pv = [&](int j) -> bool {
-                // P_j written and O rescaled (if the row maxima moved) by the softmax warps
-                if (!fa_wait(p_full, j & 1, lim)) return false;
+                // P_j stored in TMEM and O rescaled (if the row maxima moved) by the softmax warps
+                if (!fa_wait(&p_full[j & 1], (j >> 1) & 1, lim)) return false;
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + SM_V + (j & 1) * TILE);
+                const uint32_t pa = tmem + TM_P + (j & 1) * 64;
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k) {
                     const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
-                    tc_mma_f16(tmem + 256, sw128_kmajor_desc(sp + off), sw128_kmajor_desc(sv + off), idesc,
-                               (j | k) != 0);
+                    tc_mma_f16_ts(tmem + TM_O, pa + k * 8, sw128_kmajor_desc(sv + off), idesc, (j | k) != 0);
                 }
-                tc_commit(o_full);
+                tc_commit(&o_full[j & 1]);
                 tc_commit(&kv_empty[j & 1]);
                 return true;
             };
@@ -200,11 +204,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
         const int r = quad * 32 + lane;
         const int qrow = q0 + r;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-        const uint32_t oa = tmem + lane_off + 256 + hh * 64;   // this thread's half of its O row
+        const uint32_t oa = tmem + lane_off + TM_O + hh * 64;   // this thread's half of its O row
         float* red = reinterpret_cast<float*>(smem + SM_RED);     // [2][2][128]
         constexpr float RESCALE_LOG2 = 8.f;
         float m = -INFINITY, l = 0.f;
-        uint8_t* prow = smem + SM_P + hh * ATOM + r * 128;    // keys 64 hh .. 64 hh + 63 = one swizzled atom
         bool ok = true;
         for (int j = 0; j < nt; ++j) {
             const int st = j & 1, u = j >> 1;
@@ -231,11 +234,6 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             red[(st * 2 + hh) * 128 + r] = tmax;
             named_bar_sync(1 + quad, 64);
             tmax = fmaxf(tmax, red[(st * 2 + (hh ^ 1)) * 128 + r]);
-            // PV_{j-1} has completed: P may be overwritten and O is stable
-            if (j >= 1) {
-                if (ok && !fa_wait(o_full, (j - 1) & 1, lim)) ok = false;
-                tc_fence_after();
-            }
             // move the row to a new maximum only when it grew by more than 2^8
             float corr = 1.f;
             if (tmax > m + RESCALE_LOG2) {
@@ -244,6 +242,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             }
             l *= corr;
             if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+                // O rescale: PV_{j-1} must have completed
+                if (ok && !fa_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, lim)) ok = false;
+                tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 64; c += 32) {
                     float v[32];
@@ -253,40 +254,31 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                     tmem_st32(oa + c, v);
                 }
             }
-            // P = exp2(s - m) (at most 2^8) as bf16 into this half's swizzled atom; row sum
+            // P_j goes to TMEM buffer j & 1, last read by PV_{j-2}
+            if (j >= 2 && ok && !fa_wait(&o_full[st], (u - 1) & 1, lim)) ok = false;
+            // P = exp2(s - m) (at most 2^8), bf16 packed in pairs: keys 64 hh .. + 63 = columns 32 hh .. + 31
             float psum = 0.f;
+            uint32_t pk[32];
 #pragma unroll
-            for (int ch = 0; ch < 8; ++ch) {
-                float pv[8];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    pv[q] = ex2_approx(sv[8 * ch + q] - m);
-                    psum += pv[q];
-                }
-                uint4 pk;
-                __nv_bfloat162 b0 = __floats2bfloat162_rn(pv[0], pv[1]);
-                __nv_bfloat162 b1 = __floats2bfloat162_rn(pv[2], pv[3]);
-                __nv_bfloat162 b2 = __floats2bfloat162_rn(pv[4], pv[5]);
-                __nv_bfloat162 b3 = __floats2bfloat162_rn(pv[6], pv[7]);
-                pk.x = *reinterpret_cast<uint32_t*>(&b0);
-                pk.y = *reinterpret_cast<uint32_t*>(&b1);
-                pk.z = *reinterpret_cast<uint32_t*>(&b2);
-                pk.w = *reinterpret_cast<uint32_t*>(&b3);
-                *reinterpret_cast<uint4*>(prow + ((ch ^ (r & 7)) << 4)) = pk;
+            for (int i = 0; i < 32; ++i) {
+                const float p0 = ex2_approx(sv[2 * i] - m), p1 = ex2_approx(sv[2 * i + 1] - m);
+                psum += p0 + p1;
+                __nv_bfloat162 t = __floats2bfloat162_rn(p0, p1);
+                pk[i] = *reinterpret_cast<uint32_t*>(&t);
             }
+            tmem_st32_u(tmem + lane_off + TM_P + st * 64 + hh * 32, pk);
             l += psum;
-            // P visible to the tensor core (async proxy), O rescale done: PV_j may start
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            // P stored and O rescale done: PV_j may start
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
+            if (lane == 0) mbar_arrive(&p_full[st]);
         }
         // both halves' row sums (same row maximum)
         named_bar_sync(1 + quad, 64);
         red[hh * 128 + r] = l;
         named_bar_sync(1 + quad, 64);
         const float ltot = l + red[(hh ^ 1) * 128 + r];
-        if (ok && fa_wait(o_full, (nt - 1) & 1, lim)) {
+        if (ok && fa_wait(&o_full[(nt - 1) & 1], ((nt - 1) >> 1) & 1, lim)) {
             tc_fence_after();
             const float inv = 1.f / ltot;
             __nv_bfloat16* out = args.O + ((size_t)b * S + qrow) * 2048 + h * HD + hh * 64;
