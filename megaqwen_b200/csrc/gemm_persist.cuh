@@ -4,8 +4,8 @@
 // One CTA per SM walks the 128 x BN output tiles t = blockIdx.x, + gridDim.x ..
 // (BN = 256 where every B map allows it: half the A re-reads per FLOP)
 // Warp 0 (one thread) streams A/B K-slices of 64 through an mbarrier ring with
-// TMA; warp 1 owns TMEM and one of its threads issues the MMAs; warps 2-5 run
-// the epilogue.  The accumulator is double-buffered in TMEM, so the epilogue
+// TMA; warp 1 owns TMEM and one of its threads issues the MMAs; warps 2-9 run
+// the epilogue (two per TMEM lane quadrant, one per column half).  The accumulator is double-buffered in TMEM, so the epilogue
 // of tile i overlaps the MMAs of tile i + 1 and the loads run ahead across
 // tile boundaries.  Every wait is bounded and sets an error code.
 //
@@ -26,6 +26,9 @@
 namespace mq {
 
 constexpr int EPI_QKV = 4;
+
+constexpr int P_EPI_WARPS = 8;                           // two per TMEM lane quadrant
+constexpr int P_THREADS = 64 + 32 * P_EPI_WARPS;
 
 template <int EPI, int BN>
 struct PCfg {
@@ -174,7 +177,7 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
 }
 
 template <int EPI, int BN>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
+__global__ void __launch_bounds__(P_THREADS, 1)
 gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB0,
                     const __grid_constant__ CUtensorMap tmB1, const __grid_constant__ CUtensorMap tmB2,
                     const PArgs args) {
@@ -199,7 +202,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&accf[b], 1);
-            mbar_init(&acce[b], 4);
+            mbar_init(&acce[b], P_EPI_WARPS);
         }
         *abort_flag = 0;
         fence_mbar_init();
@@ -291,8 +294,10 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             }
         }
     } else {
-        // epilogue: warp w covers TMEM lanes 32 * (w % 4) .. + 31 (row of the tile)
-        const int quad = warp & 3;
+        // epilogue: warp w covers TMEM lanes 32 * (w % 4) .. + 31 (row of the tile) and
+        // column half (w - 2) / 4 of the tile
+        const int quad = warp & 3, half = (warp - 2) >> 2;
+        constexpr int HB = BN / 2;   // columns per epilogue warp
         int i = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
             const int b = i & 1, u = i >> 1;
@@ -316,12 +321,17 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         map = 2;
                     }
                 }
-#pragma unroll 1
-                for (int hd = 0; hd < BN / 128; ++hd)
-                    qkv_row_epilogue(args, acc + hd * 128, map, head * (BN / 128) + hd, row);
+                // one head per epilogue warp (BN = 256), or the two halves of one head
+                if (BN == 256) {
+                    qkv_row_epilogue(args, acc + half * 128, map, head * 2 + half, row);
+                } else {
+                    // BN = 128: the partner warp stays idle for this tile
+                    if (half == 0) qkv_row_epilogue(args, acc, map, head, row);
+                }
             } else {
-                const int n0 = nt_all * BN;
-                for (int c = 0; c < BN; c += 32) {
+                const int n0 = nt_all * BN + half * HB;
+                for (int c0 = 0; c0 < HB; c0 += 32) {
+                    const int c = half * HB + c0;
                     float v[32];
                     tmem_ld32(acc + c, v);
                     if (EPI == EPI_SILU_MUL) {
@@ -332,7 +342,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     }
                     if (row < args.M) {
                         if (EPI == EPI_STORE_F32 || EPI == EPI_ADD_F32) {
-                            float* out = reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + n0 + c;
+                            float* out = reinterpret_cast<float*>(args.C) + (size_t)row * args.ldc + n0 + c0;
 #pragma unroll
                             for (int q = 0; q < 32; q += 4) {
                                 float4 o = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
@@ -344,7 +354,7 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                             }
                         } else {
                             __nv_bfloat16* out =
-                                reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + n0 + c;
+                                reinterpret_cast<__nv_bfloat16*>(args.C) + (size_t)row * args.ldc + n0 + c0;
 #pragma unroll
                             for (int q = 0; q < 32; q += 8) *reinterpret_cast<uint4*>(out + q) = pack8_bf16(v + q);
                         }

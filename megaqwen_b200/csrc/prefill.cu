@@ -90,7 +90,7 @@ int launch_persist_bn(const void* A, int lda, const void* const* Bm, const int* 
     a.timeout_cycles = 4000000000ll;  // ~2 s at 1.9 GHz
     const int ntiles = a.tiles_m * a.tiles_n;
     const int grid = ntiles < num_sms() ? ntiles : num_sms();
-    gemm_persist_kernel<EPI, BN><<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb[0], tb[1], tb[2], a);
+    gemm_persist_kernel<EPI, BN><<<grid, P_THREADS, Cfg::SMEM, stream>>>(ta, tb[0], tb[1], tb[2], a);
     return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
 }
 
