@@ -1,6 +1,5 @@
-// Prefill kernels around the tcgen05 GEMM: embedding gather, RMSNorm to bf16,
-// QK-norm + RoPE + K/V cache write, causal GQA flash attention on the tensor
-// cores (mma.sync m16n8k16 bf16 -> fp32), and argmax.
+// Prefill kernels around the tcgen05 GEMMs and attention: embedding gather,
+// RMSNorm to bf16 and argmax.
 //
 // The kernels begin with pdl_wait/pdl_trigger so that the batched decode can
 // launch them as programmatic dependents (no-ops in an ordinary launch).
@@ -84,85 +83,6 @@ static __global__ void rmsnorm_bf16_kernel(const float* __restrict__ X, const bf
             pk[e] = *reinterpret_cast<uint32_t*>(&t);
         }
         *reinterpret_cast<uint4*>(o + c) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-    }
-}
-
-// Per token: q/k heads RMSNorm (head_dim) x norm weight, rotate-half RoPE at
-// position start_pos + s; Q, K, V to bf16 operands; K, V rows into the bf16
-// cache [L, 8, max_seq, 128] of sequence b (layer offset folded into the
-// pointers).  One block of 32 warps per token: warps 0-15 q heads, 16-23 k
-// heads, 24-31 v heads; lane owns dims lane + 32j (rotate-half pairs in-lane).
-struct QkvArgs {
-    const float* qkv;        // [M, 4096] fp32: q | k | v
-    const bf16* q_norm;
-    const bf16* k_norm;
-    const bf16* cos_table;   // [max_seq, 128]
-    const bf16* sin_table;
-    bf16* Qb;                // [M, 2048]
-    bf16* Kb;                // [M, 1024]
-    bf16* Vb;                // [M, 1024]
-    bf16* k_cache;           // layer base of sequence 0
-    bf16* v_cache;
-    long long cache_seq_stride;  // elements between sequences' caches
-    int S, start_pos, max_seq_len;
-    const int* pos_dev;      // optional: position of sequence b is pos_dev[b] (batched decode, S == 1)
-    float* Qf;               // optional: fp32 q [M, 2048] instead of bf16 Qb
-};
-
-static __global__ void __launch_bounds__(1024) qknorm_rope_kernel(const QkvArgs a) {
-    pdl_wait();
-    pdl_trigger();
-    const int m = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int b = m / a.S, p = a.pos_dev ? a.pos_dev[b] : a.start_pos + (m - b * a.S);
-    const float* row = a.qkv + (size_t)m * 4096;
-    float e[4];
-    if (warp < NQ + NKV) {
-        const bool isq = warp < NQ;
-        const float* x = row + (isq ? warp * D : 2048 + (warp - NQ) * D);
-        const bf16* nw = isq ? a.q_norm : a.k_norm;
-        float ss = 0.f;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { e[j] = x[lane + 32 * j]; ss += e[j] * e[j]; }
-        ss = warp_sum(ss);
-        const float r = rsqrtf(ss / (float)D + 1e-6f);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) e[j] = e[j] * r * __bfloat162float(nw[lane + 32 * j]);
-        const bf16* cs = a.cos_table + (size_t)p * D;
-        const bf16* sn = a.sin_table + (size_t)p * D;
-        float o[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int i = lane + 32 * j;
-            const float c = __bfloat162float(cs[i]), s = __bfloat162float(sn[i]);
-            o[j] = (j < 2) ? (e[j] * c - e[j + 2] * s) : (e[j] * c + e[j - 2] * s);
-        }
-        if (isq && a.Qf) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) a.Qf[(size_t)m * 2048 + warp * D + lane + 32 * j] = o[j];
-        } else if (isq) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) a.Qb[(size_t)m * 2048 + warp * D + lane + 32 * j] = __float2bfloat16(o[j]);
-        } else {
-            const int kh = warp - NQ;
-            bf16* kc = a.k_cache + b * a.cache_seq_stride + ((size_t)kh * a.max_seq_len + p) * D;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const bf16 v = __float2bfloat16(o[j]);
-                a.Kb[(size_t)m * 1024 + kh * D + lane + 32 * j] = v;
-                kc[lane + 32 * j] = v;
-            }
-        }
-    } else {
-        const int vh = warp - NQ - NKV;
-        const float* x = row + 3072 + vh * D;
-        bf16* vc = a.v_cache + b * a.cache_seq_stride + ((size_t)vh * a.max_seq_len + p) * D;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const bf16 v = __float2bfloat16(x[lane + 32 * j]);
-            a.Vb[(size_t)m * 1024 + vh * D + lane + 32 * j] = v;
-            vc[lane + 32 * j] = v;
-        }
     }
 }
 
