@@ -29,7 +29,7 @@ namespace db {
 
 typedef __nv_bfloat16 bf16;
 constexpr int D = MQ_HEAD_DIM;
-constexpr int ATT_CHUNK = 256;       // cache positions per attention work unit (4 warps x 4 groups of 16)
+constexpr int ATT_CHUNK_MIN = 256;   // cache positions per attention work unit: 256, 512 or 1024 per step
 constexpr int PART = 132;            // floats per (unit, head): m, l, pad, pad, acc[128]
 
 __device__ __forceinline__ uint32_t movm_t(uint32_t a) {
@@ -44,7 +44,7 @@ __device__ __forceinline__ uint32_t movm_t(uint32_t a) {
 __device__ __forceinline__ int vdim(int u, int r, int g) { return 32 * u + 8 * (g >> 1) + 2 * r + (g & 1); }
 
 // One unit = (chunk c, kv head h, sequence b), 4 warps: both q heads of kv
-// head h against cache positions [c*256, min(L, c*256+256)), L = pos[b] + 1
+// head h against cache positions [c*chunk, min(L, c*chunk+chunk)), L = pos[b] + 1
 // (the row at pos[b] was written by this step's QK-norm/RoPE kernel).  Warp w
 // takes the 16-position groups w, w+4, .. of the chunk.
 //
@@ -60,8 +60,8 @@ __device__ __forceinline__ int vdim(int u, int r, int g) { return 32 * u + 8 * (
 __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict__ Qf, const bf16* __restrict__ kc,
                                                         const bf16* __restrict__ vc, const int* __restrict__ pos,
                                                         long long seq_stride, int max_seq, int C, float scale_log2,
-                                                        float* __restrict__ part, int* __restrict__ counters,
-                                                        bf16* __restrict__ out) {
+                                                        int chunk, float* __restrict__ part,
+                                                        int* __restrict__ counters, bf16* __restrict__ out) {
     __shared__ float sm_ml[4][4];
     __shared__ float sm_acc[4][2][D];
     __shared__ int s_last;
@@ -70,7 +70,7 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
     const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int L = pos[b] + 1, p0 = c * ATT_CHUNK;
+    const int L = pos[b] + 1, p0 = c * chunk;
     float* pp = part + (((size_t)b * 8 + h) * C + c) * 2 * PART;
     if (p0 >= L) {
         if (threadIdx.x < 2) {
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
         }
         return;
     }
-    const int n = min(ATT_CHUNK, L - p0);
+    const int n = min(chunk, L - p0);
     const int ngroups = (n + 15) >> 4;
     const bf16* kb = kc + b * seq_stride + ((size_t)h * max_seq + p0) * D;
     const bf16* vb = vc + b * seq_stride + ((size_t)h * max_seq + p0) * D;
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
     }
     __syncthreads();
     const int d = threadIdx.x;
-    const int nact = (L + ATT_CHUNK - 1) / ATT_CHUNK;   // chunks holding positions of this sequence
+    const int nact = (L + chunk - 1) / chunk;   // chunks holding positions of this sequence
     bf16* o = out + (size_t)b * 2048 + (2 * h) * D + d;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -341,7 +341,7 @@ int np_of(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : B <= 64 ? 64 : 128; }
 
 Layout layout(int B, int max_seq) {
     const size_t NP = (size_t)np_of(B);
-    const int C = (max_seq + ATT_CHUNK - 1) / ATT_CHUNK;
+    const int C = (max_seq + ATT_CHUNK_MIN - 1) / ATT_CHUNK_MIN;
     Layout L;
     size_t o = 0;
     auto take = [&](size_t bytes) { size_t r = o; o += (bytes + 1023) & ~size_t(1023); return r; };
@@ -525,7 +525,12 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
     bf16* act = (bf16*)(ws + L.act);
     unsigned long long* best = (unsigned long long*)(ws + L.best);
     const int NP = np_of(B);
-    const int C = (p->max_context + ATT_CHUNK - 1) / ATT_CHUNK;
+    // the largest unit (256 / 512 / 1024 positions) that still gives >= 512 units over the
+    // (bucketed, up to 2x) context: long
+    // units amortise the unit's start-up and merge, enough of them keep every SM busy
+    int chunk = 1024;
+    while (chunk > ATT_CHUNK_MIN && (long long)B * 8 * ((p->max_context + chunk - 1) / chunk) < 512) chunk >>= 1;
+    const int C = (p->max_context + chunk - 1) / chunk;
     if (C < 1 || p->max_context > p->max_seq_len) return MQ_ERR_INVALID_ARGUMENT;
     const int norm_blocks = (B + 7) / 8;
     cudaError_t e = cudaSuccess;
@@ -560,7 +565,7 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
         if (rc) return rc;
         ok(launch(attn_unit_kernel, dim3(C, 8, B), dim3(128), 0, st, (const float*)Qf, (const bf16*)kc_l,
                   (const bf16*)vc_l, (const int*)p->positions, p->cache_seq_stride, p->max_seq_len, C,
-                  p->attn_scale * 1.4426950408889634f, part, counters, attn));
+                  p->attn_scale * 1.4426950408889634f, chunk, part, counters, attn));
         const void* wo[1] = {W.o_proj_weight};
         const int no[1] = {1024};
         a = ga;
