@@ -526,8 +526,8 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
     unsigned long long* best = (unsigned long long*)(ws + L.best);
     const int NP = np_of(B);
     // the largest unit (256 / 512 / 1024 positions) that still gives >= 512 units over the
-    // (bucketed, up to 2x) context: long
-    // units amortise the unit's start-up and merge, enough of them keep every SM busy
+    // (bucketed, up to 2x) context: long units amortise a unit's start-up and merge,
+    // enough of them keep every SM busy
     int chunk = 1024;
     while (chunk > ATT_CHUNK_MIN && (long long)B * 8 * ((p->max_context + chunk - 1) / chunk) < 512) chunk >>= 1;
     const int C = (p->max_context + chunk - 1) / chunk;
