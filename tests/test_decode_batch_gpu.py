@@ -157,3 +157,41 @@ def test_decode_step_batched_entrypoint():
         assert torch.equal(out_a.cpu(), out_b.cpu())
         toks = out_a.cpu()
     assert a.positions().cpu().tolist() == [5] * B
+
+
+@pytest.mark.parametrize("batch,length", [(16, 1600), (64, 1200)])
+def test_batch_long_context_units_match_oracle(batch, length):
+    """Long contexts select 512- and 1024-position attention units (and their
+    multi-unit merge); checked sequences follow the oracle, the others carry
+    random caches at long positions so the grid is full."""
+    L, MS = 1, 2048
+    g = torch.Generator().manual_seed(batch + length)
+    checked = (0, batch // 2, batch - 1)
+    oracles = {b: make_oracle(L, MS) for b in checked}
+    prompts = {b: torch.randint(0, 151936, (length - 37 * i,), generator=g).tolist() for i, b in enumerate(checked)}
+    bd = make_batch(L, MS, batch, use_graph=False)
+    kc, vc = bd.get_k_cache(), bd.get_v_cache()
+    kc.normal_()
+    vc.normal_()
+    pos = torch.randint(length - 200, length, (batch,), generator=g)
+    toks = torch.randint(0, 151936, (batch,), generator=g)
+    for b in checked:
+        pr = prompts[b]
+        oracles[b].prefill(pr[:-1])
+        n = len(pr) - 1
+        kc[b, :, :, :n].copy_(oracles[b].k_cache[:, :, :n].to(kc.device))
+        vc[b, :, :, :n].copy_(oracles[b].v_cache[:, :, :n].to(vc.device))
+        pos[b] = n
+        toks[b] = pr[-1]
+    bd.set_state(toks, pos)
+    for step in range(2):
+        bd.step(True)
+        bd.check()
+        logits = bd.logits().cpu()
+        out = bd.tokens().cpu().tolist()
+        for b in checked:
+            ref = oracles[b].decode_step(int(toks[b]), int(pos[b]))
+            assert_logits_close(logits[b], ref, f"B={batch} seq {b} pos {int(pos[b])}")
+            assert_token_consistent(out[b], logits[b], ref, f"B={batch} seq {b}")
+        toks = torch.tensor(out)
+        pos = pos + 1
