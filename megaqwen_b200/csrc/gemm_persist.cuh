@@ -40,6 +40,7 @@ struct PCfg {
     static constexpr int TMEM_COLS = 2 * ACC_COLS;                    // double-buffered
     static constexpr int SMEM = NSTAGES * STAGE + 1024 + 256;
     static_assert(TMEM_COLS <= 512, "two accumulator buffers fit in TMEM");
+    static_assert(BN * NB <= 256, "one MMA covers the stacked B tiles (N <= 256)");
 };
 
 struct QkvPrefillEpi {
@@ -259,7 +260,9 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN);
+            // gate/up: the two B tiles are stacked in shared memory (gate rows, then up rows), so one
+            // MMA with N = 2 BN fills both accumulators (gate at columns 0.., up at BN..)
+            constexpr uint32_t idesc = idesc_bf16_f32(GEMM_BM, BN * Cfg::NB);
             uint32_t g = 0;
             int i = 0;
             for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++i) {
@@ -284,9 +287,6 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     for (int k = 0; k < GEMM_BK / 16; ++k) {
                         const uint64_t ad = sw128_kmajor_desc(sa + k * 32);
                         tc_mma_f16(acc, ad, sw128_kmajor_desc(sa + GEMM_TILE_BYTES + k * 32), idesc, (kb | k) != 0);
-                        if (Cfg::NB == 2)
-                            tc_mma_f16(acc + BN, ad, sw128_kmajor_desc(sa + GEMM_TILE_BYTES + Cfg::B_BYTES + k * 32),
-                                       idesc, (kb | k) != 0);
                     }
                     tc_commit(&empty[s]);
                 }
