@@ -2,8 +2,9 @@
 // (tcgen05, accumulators in TMEM).
 //
 // One CTA = (block of 128 query rows, q head, sequence); 320 threads:
-//   warp 0      TMA producer: Q once, then K and V^T tiles of 128 keys into a
-//               2-stage ring;
+//   warp 0      TMA producers: lane 0 loads Q once, then K tiles of 128 keys
+//               into a 3-stage ring (a stage is freed as soon as S_j is
+//               done); lane 1 loads the V^T tiles into a 2-stage ring;
 //   warp 1      TMEM owner; one thread issues the MMAs:
 //                 S_j = Q K_j^T  (M=128 queries, N=128 keys, K=128 dims) into
 //                                 one of two S buffers,
@@ -39,10 +40,11 @@ constexpr int HD = 128;                     // head dim
 constexpr int ATOM = 128 * 128;             // bytes of a 128-row x 64-element swizzled atom (16 KB)
 constexpr int TILE = 2 * ATOM;              // a 128 x 128 bf16 operand (32 KB)
 constexpr int SM_Q = 0;
-constexpr int SM_K = SM_Q + TILE;           // [2] stages
-constexpr int SM_V = SM_K + 2 * TILE;       // [2] stages (V^T)
-constexpr int SM_BAR = SM_V + 2 * TILE;
-constexpr int SM_RED = SM_BAR + 128;        // fp32 [2 tiles][2 halves][128 rows] row maxima
+constexpr int KST = 3, VST = 2;             // K and V^T ring depths (separate rings: K is freed after S_j)
+constexpr int SM_K = SM_Q + TILE;           // [KST] stages
+constexpr int SM_V = SM_K + KST * TILE;     // [VST] stages (V^T)
+constexpr int SM_BAR = SM_V + VST * TILE;
+constexpr int SM_RED = SM_BAR + 256;        // fp32 [2 tiles][2 halves][128 rows] row maxima
 constexpr int SMEM = SM_RED + 2 * 2 * 128 * 4 + 1024;   // + barriers, row-max exchange, alignment slack
 constexpr int SOFT_WARPS = 8;               // two warps per TMEM lane quadrant, one per column half
 constexpr int THREADS = 64 + 32 * SOFT_WARPS;
@@ -81,13 +83,15 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
     uint64_t* q_full = bars + 0;
-    uint64_t* kv_full = bars + 1;     // [2]
-    uint64_t* kv_empty = bars + 3;    // [2]
-    uint64_t* s_full = bars + 5;      // [2]
-    uint64_t* s_free = bars + 7;      // [2]
-    uint64_t* p_full = bars + 9;      // [2] P_j stored on p_full[j & 1] (one barrier per P buffer)
-    uint64_t* o_full = bars + 11;     // [2] PV_j completion on o_full[j & 1]
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 13);
+    uint64_t* k_full = bars + 1;      // [KST]
+    uint64_t* k_empty = bars + 4;     // [KST]
+    uint64_t* v_full = bars + 7;      // [VST]
+    uint64_t* v_empty = bars + 9;     // [VST]
+    uint64_t* s_full = bars + 11;     // [2]
+    uint64_t* s_free = bars + 13;     // [2]
+    uint64_t* p_full = bars + 15;     // [2] P_j stored on p_full[j & 1] (one barrier per P buffer)
+    uint64_t* o_full = bars + 17;     // [2] PV_j completion on o_full[j & 1]
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 19);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int S = args.S;
@@ -101,9 +105,13 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        for (int i = 0; i < KST; ++i) {
+            mbar_init(&k_full[i], 1);
+            mbar_init(&k_empty[i], 1);
+        }
         for (int i = 0; i < 2; ++i) {
-            mbar_init(&kv_full[i], 1);
-            mbar_init(&kv_empty[i], 1);
+            mbar_init(&v_full[i], 1);
+            mbar_init(&v_empty[i], 1);
             mbar_init(&s_full[i], 1);
             mbar_init(&s_free[i], SOFT_WARPS);
         }
@@ -127,27 +135,38 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     const uint32_t tmem = *tmem_holder;
 
     if (warp == 0) {
+        const int row0 = b * S;
         if (lane == 0) {
-            const int row0 = b * S;
             mbar_arrive_expect_tx(q_full, TILE);
             tma_load_2d(smem + SM_Q, &tmQ, h * HD, row0 + q0, q_full);
             tma_load_2d(smem + SM_Q + ATOM, &tmQ, h * HD + 64, row0 + q0, q_full);
             for (int j = 0; j < nt; ++j) {
-                const int st = j & 1, u = j >> 1;
-                if (u >= 1 && !fa_wait(&kv_empty[st], (u - 1) & 1, lim)) {
+                const int st = j % KST, u = j / KST;
+                if (u >= 1 && !fa_wait(&k_empty[st], (u - 1) & 1, lim)) {
                     *abort_flag = 1;
                     atomicExch(args.err, 41);
                     break;
                 }
                 if (*abort_flag) break;
                 uint8_t* kd = smem + SM_K + st * TILE;
+                mbar_arrive_expect_tx(&k_full[st], TILE);
+                tma_load_2d(kd, &tmK, kvh * HD, row0 + j * BK, &k_full[st]);
+                tma_load_2d(kd + ATOM, &tmK, kvh * HD + 64, row0 + j * BK, &k_full[st]);
+            }
+        } else if (lane == 1) {
+            const int vrow = (b * 8 + kvh) * HD;
+            for (int j = 0; j < nt; ++j) {
+                const int st = j & 1, u = j >> 1;
+                if (u >= 1 && !fa_wait(&v_empty[st], (u - 1) & 1, lim)) {
+                    *abort_flag = 1;
+                    atomicExch(args.err, 44);
+                    break;
+                }
+                if (*abort_flag) break;
                 uint8_t* vd = smem + SM_V + st * TILE;
-                mbar_arrive_expect_tx(&kv_full[st], 2 * TILE);
-                tma_load_2d(kd, &tmK, kvh * HD, row0 + j * BK, &kv_full[st]);
-                tma_load_2d(kd + ATOM, &tmK, kvh * HD + 64, row0 + j * BK, &kv_full[st]);
-                const int vrow = (b * 8 + kvh) * HD;
-                tma_load_2d(vd, &tmV, j * BK, vrow, &kv_full[st]);
-                tma_load_2d(vd + ATOM, &tmV, j * BK + 64, vrow, &kv_full[st]);
+                mbar_arrive_expect_tx(&v_full[st], TILE);
+                tma_load_2d(vd, &tmV, j * BK, vrow, &v_full[st]);
+                tma_load_2d(vd + ATOM, &tmV, j * BK + 64, vrow, &v_full[st]);
             }
         }
     } else if (warp == 1) {
@@ -159,6 +178,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             auto pv = [&](int j) -> bool {
                 // P_j stored in TMEM and O rescaled (if the row maxima moved) by the softmax warps
                 if (!fa_wait(&p_full[j & 1], (j >> 1) & 1, lim)) return false;
+                if (!fa_wait(&v_full[j & 1], (j >> 1) & 1, lim)) return false;
                 tc_fence_after();
                 const uint32_t sv = smem_u32(smem + SM_V + (j & 1) * TILE);
                 const uint32_t pa = tmem + TM_P + (j & 1) * 64;
@@ -168,18 +188,18 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                     tc_mma_f16_ts(tmem + TM_O, pa + k * 8, sw128_kmajor_desc(sv + off), idesc, (j | k) != 0);
                 }
                 tc_commit(&o_full[j & 1]);
-                tc_commit(&kv_empty[j & 1]);
+                tc_commit(&v_empty[j & 1]);
                 return true;
             };
             for (int j = 0; ok && j < nt; ++j) {
-                const int st = j & 1, u = j >> 1;
-                if (!fa_wait(&kv_full[st], u & 1, lim) || (u >= 1 && !fa_wait(&s_free[st], (u - 1) & 1, lim)) ||
-                    *abort_flag) {
+                const int st = j & 1, u = j >> 1, kst = j % KST;
+                if (!fa_wait(&k_full[kst], (j / KST) & 1, lim) ||
+                    (u >= 1 && !fa_wait(&s_free[st], (u - 1) & 1, lim)) || *abort_flag) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t sk = smem_u32(smem + SM_K + st * TILE);
+                const uint32_t sk = smem_u32(smem + SM_K + kst * TILE);
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k) {
                     const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
@@ -187,6 +207,7 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                                k != 0);
                 }
                 tc_commit(&s_full[st]);
+                tc_commit(&k_empty[kst]);   // K_j read: its stage can take K_{j+KST}
                 if (j >= 1 && !pv(j - 1)) {
                     ok = false;
                     break;
