@@ -24,7 +24,8 @@
 //               the end.
 // All operands are K-major: Q [q][d], K [key][d], P [q][key] (TMEM) and V^T [d][key]
 // (the QKV GEMM epilogue writes V transposed per sequence and kv head).
-// Scores are in the log2 domain.  Every wait is bounded and sets an error code.
+// Scores are in the log2 domain: the QKV epilogue stores q pre-multiplied by
+// the attention scale x log2 e.  Every wait is bounded and sets an error code.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -55,10 +56,18 @@ constexpr uint32_t TM_O = 256, TM_P = 384;
 struct Args {
     __nv_bfloat16* O;       // [M, 2048] bf16, row m = b * S + s
     int S;                  // sequence length
-    float scale_log2;
     int* err;
     long long timeout_cycles;
+    unsigned long long* trace;   // optional: %globaltimer stamps of block (0,0,0), softmax warp 2, tiles < 32
 };
+
+__device__ __forceinline__ void fa_stamp(const Args& a, int j, int k) {
+    if (a.trace && j < 32 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x == 64) {
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+        a.trace[j * 8 + k] = t;
+    }
+}
 
 // 2^x on the special-function unit (ex2.approx.ftz: 2^-inf = 0)
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -234,7 +243,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             const int st = j & 1, u = j >> 1;
             // after a failed wait the loop still runs to the end (without waiting) so that the
             // partner warp's named barriers are always matched
+            fa_stamp(args, j, 0);
             if (ok && (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag)) ok = false;
+            fa_stamp(args, j, 1);
             tc_fence_after();
             const int k0 = j * BK + hh * 64;
             float sv[64];
@@ -244,17 +255,27 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&s_free[st]);
+            fa_stamp(args, j, 2);
+            // scores are already in the log2 domain (q is stored pre-scaled); only the diagonal
+            // tile and a tile past the sequence end need the causal / length mask
             float tmax = -INFINITY;
+            if (j == qb || (j + 1) * BK > S) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                const int key = k0 + i;
-                sv[i] = (key > qrow || key >= S) ? -INFINITY : sv[i] * args.scale_log2;
-                tmax = fmaxf(tmax, sv[i]);
+                for (int i = 0; i < 64; ++i) {
+                    const int key = k0 + i;
+                    sv[i] = (key > qrow || key >= S) ? -INFINITY : sv[i];
+                    tmax = fmaxf(tmax, sv[i]);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) tmax = fmaxf(tmax, sv[i]);
             }
             // row maximum over both halves (partner warp w +- 4 shares the lane quadrant)
             red[(st * 2 + hh) * 128 + r] = tmax;
+            fa_stamp(args, j, 3);
             named_bar_sync(1 + quad, 64);
             tmax = fmaxf(tmax, red[(st * 2 + (hh ^ 1)) * 128 + r]);
+            fa_stamp(args, j, 4);
             // move the row to a new maximum only when it grew by more than 2^8
             float corr = 1.f;
             if (tmax > m + RESCALE_LOG2) {
@@ -287,7 +308,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                 __nv_bfloat162 t = __floats2bfloat162_rn(p0, p1);
                 pk[i] = *reinterpret_cast<uint32_t*>(&t);
             }
+            fa_stamp(args, j, 5);
             tmem_st32_u(tmem + lane_off + TM_P + st * 64 + hh * 32, pk);
+            fa_stamp(args, j, 6);
             l += psum;
             // P stored and O rescale done: PV_j may start
             tc_fence_before();

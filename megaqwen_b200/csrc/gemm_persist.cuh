@@ -57,6 +57,7 @@ struct QkvPrefillEpi {
     int S, start_pos, max_seq;
     __nv_bfloat16* Vt;                // optional: V transposed per (sequence, kv head): [B * 8 * 128, ldvt]
     int ldvt;
+    float q_scale;                    // q is stored pre-multiplied (attention scale x log2 e)
 };
 
 struct PArgs {
@@ -133,6 +134,7 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
     const __nv_bfloat16* nw = map == 0 ? e.q_norm : e.k_norm;
     const __nv_bfloat16* cs = e.cos_table + (size_t)p * 128;
     const __nv_bfloat16* sn = e.sin_table + (size_t)p * 128;
+    const float osc = map == 0 ? e.q_scale : 1.f;
     // rotate-half pairs (d, d + 64): chunk c with chunk c + 64; weights, cos and
     // sin rows are read 8 bf16 at a time
 #pragma unroll 1
@@ -161,8 +163,8 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
                 const float ss2 = (j & 1) ? bf16hi(s2v[h]) : bf16lo(s2v[h]);
                 const float a1 = x1[i + j] * r * nw1;
                 const float a2 = x2[i + j] * r * nw2;
-                o1[j] = a1 * cc1 - a2 * ss1;
-                o2[j] = a2 * cc2 + a1 * ss2;
+                o1[j] = (a1 * cc1 - a2 * ss1) * osc;
+                o2[j] = (a2 * cc2 + a1 * ss2) * osc;
             }
             if (valid) {
                 const uint4 p1 = pack8_bf16(o1), p2 = pack8_bf16(o2);

@@ -7,6 +7,7 @@
 
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -156,6 +157,8 @@ extern "C" int mq_gemm_bf16(const void* A, int lda, const void* B, int ldb, cons
 namespace mq {
 namespace {
 
+unsigned long long* g_fa_trace = nullptr;
+
 struct PrefillLayout {
     size_t X, Xn, Qb, Kb, Vb, Vt, Ob, act, lastn, logits, err, total;
 };
@@ -253,6 +256,7 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             e.max_seq = p->max_seq_len;
             e.Vt = Vt;
             e.ldvt = ldvt;
+            e.q_scale = scale_log2;
             const void* Bm[3] = {W.q_proj_weight, W.k_proj_weight, W.v_proj_weight};
             const int Nm[3] = {2048, 1024, 1024};
             MQ_TRY(launch_persist<EPI_QKV>(Xn, 1024, Bm, Nm, 3, 1024, nullptr, 0, M, 1024, &e, err, st));
@@ -261,9 +265,18 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             fa::Args fa_args;
             fa_args.O = Ob;
             fa_args.S = S;
-            fa_args.scale_log2 = scale_log2;
             fa_args.err = err;
             fa_args.timeout_cycles = 4000000000ll;
+            fa_args.trace = nullptr;
+            {
+                // profiling hook: MQ_FA_TRACE=<layer> stamps one attention block of that layer
+                static const int at = [] { const char* e = getenv("MQ_FA_TRACE"); return e ? atoi(e) : -1; }();
+                if (at == l) {
+                    if (!g_fa_trace) cudaMalloc(&g_fa_trace, 32 * 8 * sizeof(unsigned long long));
+                    cudaMemsetAsync(g_fa_trace, 0, 32 * 8 * sizeof(unsigned long long), st);
+                    fa_args.trace = g_fa_trace;
+                }
+            }
             dim3 fgrid((S + fa::BQ - 1) / fa::BQ, MQ_NUM_Q_HEADS, B);
             fa::fa_tc_kernel<<<fgrid, fa::THREADS, fa::SMEM, st>>>(tmQ, tmK, tmV, fa_args);
         }
@@ -376,5 +389,12 @@ void launch_prefill_megakernel(const int* token_ids, int* output_token_id, int s
 }
 
 int mq_prefill_get_last_error(void) { return g_pf_last_error; }
+
+// Copies the attention trace stamps of the last MQ_FA_TRACE prefill (profiling).
+int mq_debug_fa_trace(unsigned long long* host, int n) {
+    if (!mq::g_fa_trace) return 0;
+    cudaMemcpy(host, mq::g_fa_trace, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    return n;
+}
 
 }  // extern "C"
