@@ -226,6 +226,25 @@ __device__ __forceinline__ bool global_error(const KParams& P) { return ld_relax
 // A lane reading 8-groups l, l+32, ... then issues conflict-free 16-byte loads.
 __device__ __forceinline__ int planar_index(int i, int K) { return ((i >> 2) & 1) * (K >> 1) + (i >> 3) * 4 + (i & 3); }
 
+// Two-lane fp32 accumulator for the matvecs: acc += (w pairs) * (x pairs) with
+// the packed fp32x2 FMA of sm_100 (two independent chains, half the FMAs).
+__device__ __forceinline__ unsigned long long f2pack(float a, float b) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float f2sum(unsigned long long v) {
+    float a, b;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+    return a + b;
+}
+__device__ __forceinline__ void dot8x2(unsigned long long& acc, uint4 w, float4 lo, float4 hi) {
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(f2pack(bf16lo(w.x), bf16hi(w.x))), "l"(f2pack(lo.x, lo.y)));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(f2pack(bf16lo(w.y), bf16hi(w.y))), "l"(f2pack(lo.z, lo.w)));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(f2pack(bf16lo(w.z), bf16hi(w.z))), "l"(f2pack(hi.x, hi.y)));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(f2pack(bf16lo(w.w), bf16hi(w.w))), "l"(f2pack(hi.z, hi.w)));
+}
+
 __device__ __forceinline__ float dot8(uint4 w, float4 lo, float4 hi) {
     float s = bf16lo(w.x) * lo.x;
     s = fmaf(bf16hi(w.x), lo.y, s);
@@ -870,6 +889,7 @@ struct Consumer {
                     acc[q] = 0.f;
                     up[q] = 0.f;
                     const int j = j0 + warp + NCW * q;
+                    unsigned long long a2 = 0ull, u2 = 0ull;   // fp32x2 partial sums (two chains)
                     if (j < j1) {
                         const int ti = j / T, lr = j - ti * T;
                         const uint8_t* st = g_smem + SM_STAGES + ((n + (uint32_t)(ti - g0)) % NSTAGES) * STAGE_BYTES;
@@ -881,8 +901,8 @@ struct Consumer {
                                 const int c = lane + 32 * u;
                                 const float4 lo = make_float4(xr[8 * u + 0], xr[8 * u + 1], xr[8 * u + 2], xr[8 * u + 3]);
                                 const float4 hi = make_float4(xr[8 * u + 4], xr[8 * u + 5], xr[8 * u + 6], xr[8 * u + 7]);
-                                acc[q] += dot8(w[c], lo, hi);
-                                if (KIND == 0 && phase == PH_GU) up[q] += dot8(wu[c], lo, hi);
+                                dot8x2(a2, w[c], lo, hi);
+                                if (KIND == 0 && phase == PH_GU) dot8x2(u2, wu[c], lo, hi);
                             }
                         } else {
                             const uint4* w = reinterpret_cast<const uint4*>(st + lr * K * 2);
@@ -890,10 +910,12 @@ struct Consumer {
 #pragma unroll
                             for (int u = 0; u < CPL; ++u) {
                                 const int c = lane + 32 * u;
-                                acc[q] += dot8(w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
-                                               *reinterpret_cast<const float4*>(sx() + K / 2 + c * 4));
+                                dot8x2(a2, w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
+                                       *reinterpret_cast<const float4*>(sx() + K / 2 + c * 4));
                             }
                         }
+                        acc[q] = f2sum(a2);
+                        if (KIND == 0 && phase == PH_GU) up[q] = f2sum(u2);
                     }
                 }
 #pragma unroll
