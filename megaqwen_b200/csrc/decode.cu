@@ -87,6 +87,10 @@ static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <=
               "one consumer warp per row of a tile");
 
 constexpr int BAR_CONSUMERS = 1;
+#ifndef MQ_GT_STAMPS
+#define MQ_GT_STAMPS 1
+#endif
+constexpr bool kGT = MQ_GT_STAMPS;          // %globaltimer phase/tile stamps in traced runs
 constexpr int TRACE_STRIDE = 2048;        // trace slots per CTA: phases [0,512), tiles [512, 2012)           // named barrier id for the consumer warps
 
 // ---- workspace layout (bytes) ------------------------------------------------
@@ -129,7 +133,8 @@ constexpr int SM_FLAGS = SM_BEST + 2 * NCW * 4;           // int [4]
 constexpr int SM_BARS = SM_FLAGS + 16;                    // uint64 full[NSTAGES], empty[NSTAGES]
 constexpr int SM_LAYERS = SM_BARS + 2 * NSTAGES * 8;      // LDGLayerWeights [num_layers] copy
 constexpr int SM_SCHED = SM_LAYERS + MQ_MAX_LAYERS * (int)sizeof(LDGLayerWeights);  // Sched
-constexpr int SMEM_BYTES = SM_SCHED + 128;
+constexpr int SM_PARAMS = SM_SCHED + 128;                 // KParams copy (see decode_step_kernel)
+constexpr int SMEM_BYTES = SM_PARAMS + 256;
 static_assert(SM_ACC + (NCW + 1) * 2 * D * 4 <= SM_H, "attention combine scratch fits in X+H2");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(SM_BARS % 8 == 0, "mbarrier alignment");
@@ -161,12 +166,8 @@ struct KParams {
     long long timeout_ns;
     int inject_skip_cta;
     unsigned long long* trace;
-    int poll_mode;
-    int poll_warps;
-    int poll_sleep_ns;
-    int arrive_relaxed;
-    int store_mode;
 };
+static_assert(sizeof(KParams) <= 256 && sizeof(KParams) % 4 == 0, "KParams copy fits its slot");
 
 // Per-CTA slice of every phase (identical on the producer and consumer side).
 struct Sched {
@@ -371,7 +372,7 @@ struct Producer {
             }
         }
         uint8_t* dst = smem + SM_STAGES + s * STAGE_BYTES;
-        if (P.trace && n < 320) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 512 + 4 * n] = globaltimer_ns();
+        if (kGT && P.trace && n < 320) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 512 + 4 * n] = globaltimer_ns();
         mbar_arrive_expect_tx(&full[s], (uint32_t)(b1 + b2));
         bulk_g2s(dst, src1, (uint32_t)b1, &full[s], policy);
         if (b2) bulk_g2s(dst + b1, src2, (uint32_t)b2, &full[s], policy);
@@ -440,6 +441,7 @@ struct Consumer {
     uint32_t n = 0;          // tiles consumed
     bool ok = true;          // this thread's view; made collective at begin()
     int red_par = 0;
+    float nrm = 1.f;   // rstd of the phase's RMSNorm (norm phases scale their dot products by it)
 
     __device__ static float* sx() { return sm<float>(SM_X); }
     __device__ static float* sh() { return sm<float>(SM_H); }
@@ -463,14 +465,15 @@ struct Consumer {
         ok = false;
     }
 
-    // Poll n tagged words src[idx] (idx = ct + k*NCT, k < 8) into vals; bounded.
+    // Poll `count` tagged words into registers: thread ct owns words ct + k*NCT
+    // (k < 8, eight loads in flight) and receives their values in vals.
+    // Bounded; callers synchronise X themselves.
     __device__ __forceinline__ int poll(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info) {
         int cnt = 0;
         uint32_t pending = 0;
 #pragma unroll
         for (int k = 0; k < 8; ++k)
             if (ct + k * NCT < count) { pending |= 1u << k; cnt = k + 1; }
-        if (P.poll_mode == 2) return poll_few(src, count, tag, vals, info, cnt);
         if (!ok) return cnt;
         uint64_t t0 = 0;
         uint32_t spins = 0;
@@ -485,7 +488,6 @@ struct Consumer {
                     vals[k] = __uint_as_float((uint32_t)w[k]);
                     pending &= ~(1u << k);
                 }
-            if (pending && P.poll_mode == 1) __nanosleep(P.poll_sleep_ns);
             if (pending && ((++spins & 31u) == 0)) {
                 uint64_t now = globaltimer_ns();
                 if (t0 == 0) t0 = now;
@@ -496,53 +498,8 @@ struct Consumer {
         return cnt;
     }
 
-    // Poll with only the first P.poll_warps warps, staging values through X.
-    __device__ __forceinline__ int poll_few(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info, int cnt) {
-        named_bar_sync(BAR_CONSUMERS, NCT);  // previous phase is done with X
-        const int pw = P.poll_warps;
-        if (warp < pw && ok) {
-            const int stride = pw * 32;
-            const int me = warp * 32 + lane;
-            uint64_t t0 = 0;
-            uint32_t spins = 0;
-            for (int base = 0; base < count && ok; base += 8 * stride) {
-                uint32_t pending = 0;
-#pragma unroll
-                for (int k = 0; k < 8; ++k)
-                    if (base + me + k * stride < count) pending |= 1u << k;
-                while (pending) {
-                    uint64_t w[8];
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if (pending & (1u << k)) w[k] = ld_relaxed_u64(src + base + me + k * stride);
-#pragma unroll
-                    for (int k = 0; k < 8; ++k)
-                        if ((pending & (1u << k)) && (uint32_t)(w[k] >> 32) == tag) {
-                            sx()[base + me + k * stride] = __uint_as_float((uint32_t)w[k]);
-                            pending &= ~(1u << k);
-                        }
-                    if (pending && P.poll_sleep_ns) __nanosleep(P.poll_sleep_ns);
-                    if (pending && ((++spins & 31u) == 0)) {
-                        uint64_t now = globaltimer_ns();
-                        if (t0 == 0) t0 = now;
-                        if (flags()[0] != 0 || global_error(P)) { ok = false; break; }
-                        if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, info); break; }
-                    }
-                }
-            }
-        }
-        named_bar_sync(BAR_CONSUMERS, NCT);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-            if (k < cnt) vals[k] = sx()[ct + k * NCT];
-        return cnt;
-    }
-
     __device__ __forceinline__ void ll_store(uint64_t* p, uint64_t w) {
-        if (P.store_mode == 1) asm volatile("st.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-        else if (P.store_mode == 2) asm volatile("st.global.cg.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-        else if (P.store_mode == 3) asm volatile("st.volatile.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
-        else st_relaxed_u64(p, w);
+        st_relaxed_u64(p, w);
     }
 
     // Collective: all consumer threads agree on failure.
@@ -568,25 +525,16 @@ struct Consumer {
         return s;
     }
 
-    // Store this thread's normalized K=1024 vector elements into X (planar).
-    // v[k] holds element ct + k*NCT.
-    __device__ __forceinline__ void publish_norm_1024(const float* v, float rstd, const float* wv) {
-#pragma unroll
-        for (int k = 0; k < HPT; ++k) {
-            int i = ct + k * NCT;
-            if (i < H) sx()[planar_index(i, H)] = v[k] * rstd * wv[k];
-        }
-        named_bar_sync(BAR_CONSUMERS, NCT);
-    }
-
     // Optional per-phase timestamps (profiling): slot (l*6+phase)*2 on entry,
     // +1 once the phase's input vector has arrived.
     template <int KIND>
     __device__ __forceinline__ bool begin(int phase, int l) {
         const bool tr = P.trace != nullptr && ct == 0;
-        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + (l * 6 + phase) * 2] = globaltimer_ns();
+        if (kGT && tr) P.trace[(size_t)S.c * TRACE_STRIDE + (l * 6 + phase) * 2] = globaltimer_ns();
+        micro(l, phase, 0);
         bool r = begin_impl<KIND>(phase, l);
-        if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + (l * 6 + phase) * 2 + 1] = globaltimer_ns();
+        micro(l, phase, 3);
+        if (kGT && tr) P.trace[(size_t)S.c * TRACE_STRIDE + (l * 6 + phase) * 2 + 1] = globaltimer_ns();
         return r;
     }
 
@@ -609,6 +557,7 @@ struct Consumer {
                 v[k] = 0.f;
                 wv[k] = (ct + k * NCT < H) ? __bfloat162float(w[ct + k * NCT]) : 0.f;
             }
+            named_bar_sync(BAR_CONSUMERS, NCT);   // the previous phase is done with X
             // QKV/LM: layer input h (embedding row at layer 0, else the previous
             // layer's output); GU: the post-attention residual.
             if (phase == PH_GU) {
@@ -621,17 +570,25 @@ struct Consumer {
             } else {
                 poll(ll_hout(P, l - 1), H, tag_of(S, l - 1), v, ((uint32_t)phase << 8) | l);
             }
+            micro(l, phase, 1);
             float* res = (phase == PH_GU) ? sh2() : sh();
+            // RMSNorm folded into the matvec: X holds x * w (no barrier for the
+            // sum of squares first); the phase scales each dot product by rstd.
             float ss = 0.f;
 #pragma unroll
-            for (int k = 0; k < HPT; ++k)
-                if (ct + k * NCT < H) {
-                    if (ok) res[ct + k * NCT] = v[k];
+            for (int k = 0; k < HPT; ++k) {
+                const int i = ct + k * NCT;
+                if (i < H) {
+                    if (ok) res[i] = v[k];
                     ss += v[k] * v[k];
+                    sx()[planar_index(i, H)] = v[k] * wv[k];
                 }
+            }
             block_sum(ss);
-            if (!agree()) return false;
-            float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
+            if (!agree()) return false;   // publishes X and the per-warp sums
+            micro(l, phase, 2);
+            const float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
+            nrm = rstd;
             if (phase == PH_LM && S.c == 0) {
 #pragma unroll
                 for (int k = 0; k < HPT; ++k) {
@@ -641,20 +598,21 @@ struct Consumer {
                     if (P.norm_out) P.norm_out[i] = v[k] * rstd * wv[k];
                 }
             }
-            publish_norm_1024(v, rstd, wv);
             return true;
         }
         if (KIND == 3) {
             const int K = (phase == PH_O) ? QS : I;
             const uint64_t* src = (phase == PH_O) ? ll_attn(P, l) : ll_act(P, l);
+            named_bar_sync(BAR_CONSUMERS, NCT);   // the previous phase is done with X
             int cnt = poll(src, K, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
-            if (!agree()) return false;
+            micro(l, phase, 1);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
                 int i = ct + k * NCT;
                 if (k < cnt && i < K) sx()[planar_index(i, K)] = v[k];
             }
-            named_bar_sync(BAR_CONSUMERS, NCT);
+            if (!agree()) return false;   // publishes X
+            micro(l, phase, 2);
             return true;
         }
         // PH_ATTN: raw q (2 heads), k, v of kv head g -> smem, then QK-norm + RoPE.
@@ -765,7 +723,9 @@ struct Consumer {
         if (!ok) return false;
         uint64_t t0 = 0;
         uint32_t spins = 0;
-        while (!__all_sync(0xffffffffu, mbar_try_wait(&full()[s], par))) {
+        // one lane per warp polls: 480 threads polling one mbarrier serialise
+        // at the barrier (~300 cycles per poll even when the phase is done)
+        while (!__shfl_sync(0xffffffffu, lane == 0 ? (int)mbar_try_wait(&full()[s], par) : 0, 0)) {
             if ((++spins & 63u) == 0) {
                 int verdict = 0;
                 if (lane == 0) {
@@ -783,6 +743,7 @@ struct Consumer {
                 }
             }
         }
+        __syncwarp();   // lane 0's acquire of the stage orders the other lanes' reads after it
         return true;
     }
 
@@ -834,6 +795,7 @@ struct Consumer {
                 xr[8 * u + 4] = hi.x; xr[8 * u + 5] = hi.y; xr[8 * u + 6] = hi.z; xr[8 * u + 7] = hi.w;
             }
         }
+        micro(l, phase, 4);
         if (KIND == 2) {
             LmBest best{-INFINITY, 0x7fffffff};
             mv_phase<2, PH_LM>(l, xr, &best);
@@ -874,13 +836,14 @@ struct Consumer {
         for (int g0 = 0; g0 < ntiles; g0 += MV_GROUP) {
             const int g1 = min(ntiles, g0 + MV_GROUP);
             const bool tr = P.trace && ct == 0 && n < 320;
-            if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 513 + 4 * n] = globaltimer_ns();
+            if (kGT && tr) P.trace[(size_t)S.c * TRACE_STRIDE + 513 + 4 * n] = globaltimer_ns();
             bool got = true;
             for (int i = g0; i < g1; ++i) {
                 const uint32_t t = n + (uint32_t)(i - g0);
                 got = wait_full(t % NSTAGES, (t / NSTAGES) & 1u, phase, l) && got;
             }
-            if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 514 + 4 * n] = globaltimer_ns();
+            if (kGT && tr) P.trace[(size_t)S.c * TRACE_STRIDE + 514 + 4 * n] = globaltimer_ns();
+            if (g0 == 0) micro(l, phase, 5);
             const int j0 = g0 * T, j1 = min(g1 * T, R);
             if (got) {
                 float acc[MV_Q], up[MV_Q];
@@ -918,6 +881,7 @@ struct Consumer {
                         if (KIND == 0 && phase == PH_GU) up[q] = f2sum(u2);
                     }
                 }
+                if (g0 == 0) micro(l, phase, 6);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
 #pragma unroll
@@ -926,18 +890,19 @@ struct Consumer {
                         if (KIND == 0 && phase == PH_GU) up[q] += __shfl_xor_sync(0xffffffffu, up[q], o);
                     }
                 }
+                if (g0 == 0) micro(l, phase, 7);
                 if (lane == 0) {
 #pragma unroll
                     for (int q = 0; q < MV_Q; ++q) {
                         const int j = j0 + warp + NCW * q;
                         if (j >= j1) continue;
                         const int r = a + j;
-                        const float v = acc[q];
+                        const float v = (KIND == 0 || KIND == 2) ? acc[q] * nrm : acc[q];
                         if (KIND == 2) {
                             if (P.logits) P.logits[r] = v;
                             if (v > bst->v || (v == bst->v && r < bst->i)) { bst->v = v; bst->i = r; }
                         } else if (phase == PH_GU) {
-                            ll_store(ll_act(P, l) + r, ll_word(v / (1.0f + expf(-v)) * up[q], tag));
+                            ll_store(ll_act(P, l) + r, ll_word(v / (1.0f + expf(-v)) * (up[q] * nrm), tag));
                         } else if (phase == PH_QKV) {
                             if (!((S.c == P.inject_skip_cta - 1) && l == 0)) ll_store(ll_qkv(P, l) + r, ll_word(v, tag));
                         } else if (phase == PH_O) {
@@ -947,8 +912,10 @@ struct Consumer {
                         }
                     }
                 }
-                if (tr) P.trace[(size_t)S.c * TRACE_STRIDE + 515 + 4 * n] = globaltimer_ns();
+                if (g0 == 0) micro(l, phase, 8);
+                if (kGT && tr) P.trace[(size_t)S.c * TRACE_STRIDE + 515 + 4 * n] = globaltimer_ns();
                 for (int i = g0; i < g1; ++i) release((n + (uint32_t)(i - g0)) % NSTAGES);
+                if (g0 == 0) micro(l, phase, 9);
             }
             n += (uint32_t)(g1 - g0);
         }
@@ -1056,20 +1023,23 @@ struct Consumer {
     __device__ __forceinline__ void release(uint32_t s) {
         __syncwarp();
         if (lane == 0) {
-            if (P.arrive_relaxed) mbar_arrive_relaxed(&empty()[s]);
-            else mbar_arrive(&empty()[s]);
+            mbar_arrive_relaxed(&empty()[s]);
         }
     }
 
     // Trace slots 340 + 5 l + k of the attention phase (k: 0 q fragments built,
     // 1 start of tiles, 2 tiles done, 3 local merge done, 4 phase done),
     // consumer thread 0.
+    // clock64 micro-stamps inside the phases of layer 14 (slots 1792 + phase*24 + k)
+    __device__ __forceinline__ void micro(int l, int phase, int k) {
+        if (P.trace && l == 14 && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 1792 + phase * 24 + k] = clock64();
+    }
     __device__ __forceinline__ void attn_stamp(int l, int k) {
-        if (P.trace && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 340 + 5 * l + k] = globaltimer_ns();
+        if (kGT && P.trace && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 340 + 5 * l + k] = globaltimer_ns();
     }
     // extra split-K combine stamps (layer 14 only): slots 480 + k
     __device__ __forceinline__ void comb_stamp(int l, int k) {
-        if (P.trace && l == 14 && (threadIdx.x & 31) == 0 && warp == 0)
+        if (kGT && P.trace && l == 14 && (threadIdx.x & 31) == 0 && warp == 0)
             P.trace[(size_t)S.c * TRACE_STRIDE + 480 + k] = globaltimer_ns();
     }
 
@@ -1359,20 +1329,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_c
         const int words = P.num_layers * (int)(sizeof(LDGLayerWeights) / 8);
         for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
     }
+    {
+        // The phases read their parameters from a shared-memory copy: kernel
+        // parameters live in the constant bank, whose cache shares the SM's
+        // instruction/constant cache with this kernel's large code and misses
+        // (an L2 round trip per parameter read) between phases.
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(&P);
+        uint32_t* dst = sm<uint32_t>(SM_PARAMS);
+        for (int i = threadIdx.x; i < (int)(sizeof(KParams) / 4); i += blockDim.x) dst[i] = src[i];
+    }
     __syncthreads();
+    const KParams& Ps = *sm<KParams>(SM_PARAMS);
 
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) {
-            Producer pr(P, g_smem);
-            walk(P, S, pr);
+            Producer pr(Ps, g_smem);
+            walk(Ps, S, pr);
             if (P.trace) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 502] = globaltimer_ns();
             pr.drain();
         }
         return;
     }
-    ConsumerWalk cs{&P};
+    ConsumerWalk cs{&Ps};
     if (P.trace && threadIdx.x == 32) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 500] = globaltimer_ns();
-    walk(P, S, cs);
+    walk(Ps, S, cs);
     if (P.trace && threadIdx.x == 32) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 501] = globaltimer_ns();
 }
 
@@ -1490,22 +1470,6 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     k.timeout_ns = p->timeout_ns > 0 ? p->timeout_ns : 2000000000ll;
     k.inject_skip_cta = p->inject_skip_cta;
     k.trace = p->trace;
-    {
-        // tuning knobs, read from the environment once per process
-        struct Knobs {
-            int poll_mode, poll_warps, poll_sleep, store_mode, arrive_relaxed;
-        };
-        static const Knobs kn = [] {
-            auto env = [](const char* n, int d) { const char* e = getenv(n); return e ? atoi(e) : d; };
-            return Knobs{env("MQ_POLL_MODE", 2), env("MQ_POLL_WARPS", mq::NCW), env("MQ_POLL_SLEEP", 0),
-                         env("MQ_STORE_MODE", 0), env("MQ_ARRIVE_RELAXED", 1)};
-        }();
-        k.poll_mode = kn.poll_mode;
-        k.poll_warps = kn.poll_warps;
-        k.poll_sleep_ns = kn.poll_sleep;
-        k.store_mode = kn.store_mode;
-        k.arrive_relaxed = kn.arrive_relaxed;
-    }
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);
