@@ -132,8 +132,10 @@ typedef struct mq_decode_params {
     long long timeout_ns;          /* bound on every device wait; 0: default (2 s) */
     int inject_skip_cta;           /* test hook: CTA (value - 1) withholds its layer-0 QKV handoff
                                       stores, so the others' waits run out; 0: off */
-    unsigned long long* trace;     /* optional device buffer [num_ctas * 512] of %globaltimer
-                                      stamps per CTA and phase (profiling); NULL: off */
+    unsigned long long* trace;     /* optional device buffer [num_ctas * 2048] of %globaltimer
+                                      stamps per CTA, phase and tile (profiling); NULL: off.
+                                      Only kernel start/end are stamped unless the library was
+                                      built with MQ_DECODE_TRACE=1 (see megaqwen_b200/build.py) */
 } mq_decode_params;
 
 size_t mq_decode_workspace_bytes(void);

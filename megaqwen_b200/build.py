@@ -11,6 +11,9 @@ Outputs
 
 Run ``python megaqwen_b200/build.py`` (or ``__graft_entry__.build()``).  Each
 output is rebuilt only when a source it depends on is newer.
+``MQ_DECODE_TRACE=1 python megaqwen_b200/build.py --force`` builds the decode
+kernel with its per-phase/per-tile trace stamps (``mq_decode_params.trace``);
+the default build leaves them out.
 """
 from __future__ import annotations
 
@@ -63,6 +66,8 @@ def build_lib(verbose: bool = False, force: bool = False) -> Path:
     LIBDIR.mkdir(exist_ok=True)
     cmd = [_nvcc(), *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "-shared", "-Xcompiler", "-fPIC",
            "-Xptxas", "-v", f"-I{INCLUDE}", f"-I{CSRC}", *srcs, "-o", LIB]
+    if os.environ.get("MQ_DECODE_TRACE") == "1":
+        cmd.insert(1, "-DMQ_DECODE_TRACE=1")
     out = _run(cmd, verbose)
     (LIBDIR / "ptxas_info.txt").write_text(out)
     return LIB

@@ -87,10 +87,14 @@ static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <=
               "one consumer warp per row of a tile");
 
 constexpr int BAR_CONSUMERS = 1;
-#ifndef MQ_GT_STAMPS
-#define MQ_GT_STAMPS 1
+// In-phase trace stamps (phase, tile, attention and clock64 micro stamps) are
+// compiled only with -DMQ_DECODE_TRACE=1: their code, even when not executed,
+// spreads the hot loop over more instruction-cache lines and costs ~10 % of
+// the step.  The per-kernel start/end stamps are always available.
+#ifndef MQ_DECODE_TRACE
+#define MQ_DECODE_TRACE 0
 #endif
-constexpr bool kGT = MQ_GT_STAMPS;          // %globaltimer phase/tile stamps in traced runs
+constexpr bool kGT = MQ_DECODE_TRACE;
 constexpr int TRACE_STRIDE = 2048;        // trace slots per CTA: phases [0,512), tiles [512, 2012)           // named barrier id for the consumer warps
 
 // ---- workspace layout (bytes) ------------------------------------------------
@@ -351,7 +355,9 @@ struct Producer {
         return ok;
     }
 
-    __device__ __forceinline__ void tile(int phase, int layer, const char* src1, int b1, const char* src2, int b2) {
+    // Out of line: one copy of the issue code serves all six tile loops (a
+    // smaller producer leaves more of the instruction cache to the consumers).
+    __device__ __noinline__ void tile(int phase, int layer, const char* src1, int b1, const char* src2, int b2) {
         if (!ok) return;
         const uint32_t s = n % NSTAGES;
         if (n >= (uint32_t)NSTAGES) {
@@ -466,24 +472,25 @@ struct Consumer {
     }
 
     // Poll `count` tagged words into registers: thread ct owns words ct + k*NCT
-    // (k < 8, eight loads in flight) and receives their values in vals.
-    // Bounded; callers synchronise X themselves.
+    // (k < NK <= 8, all loads in flight at once) and receives their values in
+    // vals.  Bounded; callers synchronise X themselves.
+    template <int NK>
     __device__ __forceinline__ int poll(const uint64_t* src, int count, uint32_t tag, float* vals, uint32_t info) {
         int cnt = 0;
         uint32_t pending = 0;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
+        for (int k = 0; k < NK; ++k)
             if (ct + k * NCT < count) { pending |= 1u << k; cnt = k + 1; }
         if (!ok) return cnt;
         uint64_t t0 = 0;
         uint32_t spins = 0;
         while (pending) {
-            uint64_t w[8];
+            uint64_t w[NK];
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
+            for (int k = 0; k < NK; ++k)
                 if (pending & (1u << k)) w[k] = ld_relaxed_u64(src + ct + k * NCT);
 #pragma unroll
-            for (int k = 0; k < 8; ++k)
+            for (int k = 0; k < NK; ++k)
                 if ((pending & (1u << k)) && (uint32_t)(w[k] >> 32) == tag) {
                     vals[k] = __uint_as_float((uint32_t)w[k]);
                     pending &= ~(1u << k);
@@ -560,15 +567,16 @@ struct Consumer {
             named_bar_sync(BAR_CONSUMERS, NCT);   // the previous phase is done with X
             // QKV/LM: layer input h (embedding row at layer 0, else the previous
             // layer's output); GU: the post-attention residual.
-            if (phase == PH_GU) {
-                poll(ll_hmid(P, l), H, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
-            } else if (l == 0) {
+            if (phase != PH_GU && l == 0) {
                 const bf16* row = P.embed + (size_t)flags()[1] * H;
 #pragma unroll
                 for (int k = 0; k < HPT; ++k)
                     if (ct + k * NCT < H) v[k] = __bfloat162float(row[ct + k * NCT]);
             } else {
-                poll(ll_hout(P, l - 1), H, tag_of(S, l - 1), v, ((uint32_t)phase << 8) | l);
+                // one call site: the poll loop is inlined once per phase kind
+                const bool gu = phase == PH_GU;
+                poll<HPT>(gu ? ll_hmid(P, l) : ll_hout(P, l - 1), H, tag_of(S, gu ? l : l - 1), v,
+                          ((uint32_t)phase << 8) | l);
             }
             micro(l, phase, 1);
             float* res = (phase == PH_GU) ? sh2() : sh();
@@ -589,7 +597,7 @@ struct Consumer {
             micro(l, phase, 2);
             const float rstd = rsqrtf(read_sum() / (float)H + 1e-6f);
             nrm = rstd;
-            if (phase == PH_LM && S.c == 0) {
+            if (KIND == 2 && S.c == 0) {
 #pragma unroll
                 for (int k = 0; k < HPT; ++k) {
                     const int i = ct + k * NCT;
@@ -604,10 +612,10 @@ struct Consumer {
             const int K = (phase == PH_O) ? QS : I;
             const uint64_t* src = (phase == PH_O) ? ll_attn(P, l) : ll_act(P, l);
             named_bar_sync(BAR_CONSUMERS, NCT);   // the previous phase is done with X
-            int cnt = poll(src, K, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
+            int cnt = poll<(I + NCT - 1) / NCT>(src, K, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
             micro(l, phase, 1);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
+            for (int k = 0; k < (I + NCT - 1) / NCT; ++k) {
                 int i = ct + k * NCT;
                 if (k < cnt && i < K) sx()[planar_index(i, K)] = v[k];
             }
@@ -870,7 +878,7 @@ struct Consumer {
                         } else {
                             const uint4* w = reinterpret_cast<const uint4*>(st + lr * K * 2);
                             constexpr int CPL = K / 256;
-#pragma unroll
+#pragma unroll 2
                             for (int u = 0; u < CPL; ++u) {
                                 const int c = lane + 32 * u;
                                 dot8x2(a2, w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
@@ -1032,7 +1040,7 @@ struct Consumer {
     // consumer thread 0.
     // clock64 micro-stamps inside the phases of layer 14 (slots 1792 + phase*24 + k)
     __device__ __forceinline__ void micro(int l, int phase, int k) {
-        if (P.trace && l == 14 && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 1792 + phase * 24 + k] = clock64();
+        if (kGT && P.trace && l == 14 && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 1792 + phase * 24 + k] = clock64();
     }
     __device__ __forceinline__ void attn_stamp(int l, int k) {
         if (kGT && P.trace && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 340 + 5 * l + k] = globaltimer_ns();
