@@ -162,7 +162,7 @@ int mq_decode(const mq_decode_params* params, cudaStream_t stream);
  * leaves the output token unwritten; the scratch then holds a stale error and
  * the process should stop using this entry point on that device.  Calls no
  * cudaMalloc, cudaFree or other allocating routine. */
-#define MQ_NOALLOC_SCRATCH_BYTES 450816
+#define MQ_NOALLOC_SCRATCH_BYTES 721152
 int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream);
 /* Copy the workspace error word (and the auxiliary info word) to the host;
  * synchronises `stream`. */

@@ -66,7 +66,7 @@ constexpr int NSTAGES = 5;
 constexpr int MAX_CTAS = 256;
 constexpr int CMAX = MAX_CTAS / NKV;       // max position chunks per kv head
 static_assert(CMAX <= 32, "the split-K combine holds one unit per lane");
-constexpr int PART_STRIDE = 132;           // floats per (unit, head): m, l, pad, pad, acc[128]
+constexpr int PART_STRIDE = 132;           // tagged words per (unit, head): acc[128], m, l, pad, pad
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int QKV_TILE = cmin(NCW, STAGE_BYTES / (H * 2));      // 15 rows
@@ -106,8 +106,7 @@ struct Control {
     unsigned long long lm_best;   // packed (ordered value, ~index) running max
     int32_t last_token;
     int32_t last_position;
-    uint32_t attn_count[NKV];     // arrivals per kv head for split-K combine
-    uint32_t pad[48];
+    uint32_t pad[56];
 };
 static_assert(sizeof(Control) == 256, "control block is 256 bytes");
 
@@ -118,7 +117,7 @@ constexpr size_t OFF_HMID = OFF_ATTN + 2ull * QS * 8;
 constexpr size_t OFF_ACT = OFF_HMID + 2ull * H * 8;
 constexpr size_t OFF_HOUT = OFF_ACT + 2ull * I * 8;
 constexpr size_t OFF_PART = OFF_HOUT + 2ull * H * 8;
-constexpr size_t WS_BYTES = OFF_PART + (size_t)NKV * CMAX * 2 * PART_STRIDE * 4;
+constexpr size_t WS_BYTES = OFF_PART + (size_t)NKV * CMAX * 2 * PART_STRIDE * 8;
 
 // ---- shared memory layout (bytes, dynamic) -------------------------------------
 constexpr int SM_STAGES = 0;
@@ -215,8 +214,10 @@ __device__ __forceinline__ uint64_t* ll_act(const KParams& P, int l) {
 __device__ __forceinline__ uint64_t* ll_hout(const KParams& P, int l) {
     return reinterpret_cast<uint64_t*>(P.ws + OFF_HOUT) + (size_t)(l & 1) * H;
 }
-__device__ __forceinline__ float* part_of(const KParams& P, int g, int j, int h) {
-    return reinterpret_cast<float*>(P.ws + OFF_PART) + ((size_t)(g * CMAX + j) * 2 + h) * PART_STRIDE;
+// Split-K partial of unit j, head h of kv head g as tagged words: acc[128]
+// (unnormalised), max (log2 domain) at 128, sum at 129.
+__device__ __forceinline__ uint64_t* part_of(const KParams& P, int g, int j, int h) {
+    return reinterpret_cast<uint64_t*>(P.ws + OFF_PART) + ((size_t)(g * CMAX + j) * 2 + h) * PART_STRIDE;
 }
 
 __device__ __forceinline__ void record_error(const KParams& P, uint32_t code, uint32_t info) {
@@ -1045,11 +1046,6 @@ struct Consumer {
     __device__ __forceinline__ void attn_stamp(int l, int k) {
         if (kGT && P.trace && ct == 0) P.trace[(size_t)S.c * TRACE_STRIDE + 340 + 5 * l + k] = globaltimer_ns();
     }
-    // extra split-K combine stamps (layer 14 only): slots 480 + k
-    __device__ __forceinline__ void comb_stamp(int l, int k) {
-        if (kGT && P.trace && l == 14 && (threadIdx.x & 31) == 0 && warp == 0)
-            P.trace[(size_t)S.c * TRACE_STRIDE + 480 + k] = globaltimer_ns();
-    }
 
     __device__ __forceinline__ void end_attn(AttnState& a, int l) {
         float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);   // [16][2][128]
@@ -1107,105 +1103,110 @@ struct Consumer {
             *reinterpret_cast<float4*>(acc + (NCW * 2 + 1) * D + 4 * lane) = v4;
         }
         named_bar_sync(BAR_CONSUMERS, NCT);
-        float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
         const int h = warp;  // warps 0 and 1 combine heads 0 and 1
-        if (warp < 2) {
-            // lane w <= NCW holds entry w's (max, sum); the weights are shuffled to all lanes
-            const float mw = lane <= NCW ? ml[lane * 4 + 2 * h] : -INFINITY;
-            M = mw;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-            const float ew = mw == -INFINITY ? 0.f : exp2f(mw - M);   // entries without positions weigh 0
-            Ls = warp_sum(lane <= NCW ? ml[lane * 4 + 2 * h + 1] * ew : 0.f);
-#pragma unroll
-            for (int w = 0; w <= NCW; ++w) {
-                const float e = __shfl_sync(0xffffffffu, ew, w);
-                const float4 av = *reinterpret_cast<const float4*>(acc + (w * 2 + h) * D + 4 * lane);
-                A[0] += av.x * e; A[1] += av.y * e; A[2] += av.z * e; A[3] += av.w * e;
-            }
-        }
         const uint32_t tag = tag_of(S, l);
-        uint64_t* out = ll_attn(P, l) + 256 * S.ug;
-        if (S.C == 1) {
-            if (warp < 2 && ok) {
-                float inv = 1.0f / Ls;
+        // Pass 0 merges this unit's warps (+ the current position).  With C > 1
+        // the units j >= 1 publish that partial as tagged words and leave; unit
+        // 0 (the kv head's combiner) polls them into the same entry slots and
+        // pass 1 merges them with its own partial.
+        for (int pass = 0;; ++pass) {
+            float M = -INFINITY, Ls = 0.f, A[4] = {0.f, 0.f, 0.f, 0.f};
+            if (warp < 2) {
+                // lane w <= NCW holds entry w's (max, sum); the weights are shuffled to all lanes
+                const float mw = lane <= NCW ? ml[lane * 4 + 2 * h] : -INFINITY;
+                M = mw;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(A[i] * inv, tag));
-            }
-            return;
-        }
-        // split-K: publish the partial, the last unit of this kv head combines
-        attn_stamp(l, 3);
-        volatile int* f = flags();
-        if (warp < 2) {
-            float* pp = part_of(P, S.ug, S.uj, h);
-            if (lane == 0) { pp[0] = M; pp[1] = Ls; }
-            *reinterpret_cast<float4*>(pp + 4 + 4 * lane) = make_float4(A[0], A[1], A[2], A[3]);
-        }
-        named_bar_sync(BAR_CONSUMERS, NCT);
-        if (ct == 0) {
-            // release (cumulative over the CTA's partial stores ordered by the barrier) and acquire
-            Control* C = ctrl_of(P);
-            uint32_t old;
-            asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(old) : "l"(&C->attn_count[S.ug]) : "memory");
-            const int last = (old == (uint32_t)(S.C - 1));
-            if (last) atomicExch(&C->attn_count[S.ug], 0u);
-            f[2] = last;
-        }
-        comb_stamp(l, 0);
-        named_bar_sync(BAR_CONSUMERS, NCT);
-        comb_stamp(l, 1);
-        if (!f[2]) return;   // the flag is CTA-uniform: every consumer thread takes the same path
-        // combine the S.C partials of both heads: warp w sums units w, w + NCW, .. into
-        // shared memory (one L2 round trip for all units), warps 0/1 add the NCW sums
-        float* cs = reinterpret_cast<float*>(g_smem + SM_ACC);   // [NCW][2][128]
-        {
-            float mj[2] = {-INFINITY, -INFINITY}, lj[2] = {0.f, 0.f};
-            if (lane < S.C) {
+                for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+                const float ew = mw == -INFINITY ? 0.f : exp2f(mw - M);   // entries without positions weigh 0
+                Ls = warp_sum(lane <= NCW ? ml[lane * 4 + 2 * h + 1] * ew : 0.f);
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const float* pp = part_of(P, S.ug, lane, hh);
-                    mj[hh] = __ldcg(pp);
-                    lj[hh] = __ldcg(pp + 1);
+                for (int w = 0; w <= NCW; ++w) {
+                    const float e = __shfl_sync(0xffffffffu, ew, w);
+                    const float4 av = *reinterpret_cast<const float4*>(acc + (w * 2 + h) * D + 4 * lane);
+                    A[0] += av.x * e; A[1] += av.y * e; A[2] += av.z * e; A[3] += av.w * e;
                 }
             }
-            float gm[2], ej[2], gl[2];
+            if (S.C == 1 || pass == 1) {
+                if (warp < 2 && ok) {
+                    uint64_t* out = ll_attn(P, l) + 256 * S.ug;
+                    const float inv = 1.0f / Ls;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(A[i] * inv, tag));
+                }
+                return;
+            }
+            if (S.uj != 0) {
+                if (warp < 2 && ok) {
+                    uint64_t* pw = part_of(P, S.ug, S.uj, h);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) ll_store(pw + 4 * lane + i, ll_word(A[i], tag));
+                    if (lane == 0) {
+                        ll_store(pw + 128, ll_word(M, tag));
+                        ll_store(pw + 129, ll_word(Ls, tag));
+                    }
+                }
+                return;
+            }
+            attn_stamp(l, 3);
+            named_bar_sync(BAR_CONSUMERS, NCT);   // pass 0 is done reading the entry slots
+            if (warp < 2) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[(NCW * 2 + h) * D + 4 * lane + i] = A[i];
+                if (lane == 0) { ml[NCW * 4 + 2 * h] = M; ml[NCW * 4 + 2 * h + 1] = Ls; }
+            }
+            gather_partials(l, tag, acc, ml);
+            named_bar_sync(BAR_CONSUMERS, NCT);
+        }
+    }
+
+    // Combiner (unit 0 of a kv head, C > 1): warp w polls the tagged partials of
+    // units 1 + w, 1 + w + NCW, .. (all words of a unit in flight at once),
+    // merges them and stores the result in entry slot w (max -inf: empty).
+    __device__ __forceinline__ void gather_partials(int l, uint32_t tag, float* acc, float* ml) {
+        float mm[2] = {-INFINITY, -INFINITY}, lsum[2] = {0.f, 0.f}, am[2][4] = {};
+        for (int r = 0; r < (CMAX - 1 + NCW - 1) / NCW; ++r) {
+            const int j = 1 + warp + r * NCW;
+            if (j >= S.C) break;   // warp-uniform
+            const uint64_t* p0 = part_of(P, S.ug, j, 0);
+            const uint64_t* p1 = part_of(P, S.ug, j, 1);
+            uint64_t w[9];
+            uint32_t pending = lane < 4 ? 0x1ffu : 0xffu;
+            uint64_t t0 = 0;
+            uint32_t spins = 0;
+            while (ok && pending) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (pending & (1u << i)) w[i] = ld_relaxed_u64(p0 + 4 * lane + i);
+                    if (pending & (1u << (4 + i))) w[4 + i] = ld_relaxed_u64(p1 + 4 * lane + i);
+                }
+                if (pending & 0x100u) w[8] = ld_relaxed_u64((lane < 2 ? p0 : p1) + 128 + (lane & 1));
+#pragma unroll
+                for (int i = 0; i < 9; ++i)
+                    if ((pending & (1u << i)) && (uint32_t)(w[i] >> 32) == tag) pending &= ~(1u << i);
+                if (pending && ((++spins & 31u) == 0)) {
+                    uint64_t now = globaltimer_ns();
+                    if (t0 == 0) t0 = now;
+                    if (flags()[0] != 0 || global_error(P)) { ok = false; break; }
+                    if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, ((uint32_t)PH_ATTN << 8) | l); break; }
+                }
+            }
+            const float mlv = __uint_as_float((uint32_t)w[8]);
 #pragma unroll
             for (int hh = 0; hh < 2; ++hh) {
-                gm[hh] = mj[hh];
+                const float mj = __shfl_sync(0xffffffffu, mlv, 2 * hh), lj = __shfl_sync(0xffffffffu, mlv, 2 * hh + 1);
+                const float nm = fmaxf(mm[hh], mj);
+                const float c0 = mm[hh] == -INFINITY ? 0.f : exp2f(mm[hh] - nm), c1 = exp2f(mj - nm);
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) gm[hh] = fmaxf(gm[hh], __shfl_xor_sync(0xffffffffu, gm[hh], o));
-                ej[hh] = lane < S.C ? exp2f(mj[hh] - gm[hh]) : 0.f;   // unit maxima are in the log2 domain
-                gl[hh] = warp_sum(lj[hh] * ej[hh]);
+                for (int i = 0; i < 4; ++i) am[hh][i] = am[hh][i] * c0 + __uint_as_float((uint32_t)w[4 * hh + i]) * c1;
+                lsum[hh] = lsum[hh] * c0 + lj * c1;
+                mm[hh] = nm;
             }
-            float4 g4[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-            for (int j2 = warp; j2 < S.C; j2 += NCW) {
+        }
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    const float e = __shfl_sync(0xffffffffu, ej[hh], j2);
-                    const float4 av = __ldcg(reinterpret_cast<const float4*>(part_of(P, S.ug, j2, hh) + 4 + 4 * lane));
-                    g4[hh].x += av.x * e; g4[hh].y += av.y * e; g4[hh].z += av.z * e; g4[hh].w += av.w * e;
-                }
-            }
-            comb_stamp(l, 2);
+        for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
-            for (int hh = 0; hh < 2; ++hh) *reinterpret_cast<float4*>(cs + (warp * 2 + hh) * D + 4 * lane) = g4[hh];
-            named_bar_sync(BAR_CONSUMERS, NCT);
-            if (warp < 2) {
-                float G4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                for (int w = 0; w < NCW; ++w) {
-                    const float4 av = *reinterpret_cast<const float4*>(cs + (w * 2 + h) * D + 4 * lane);
-                    G4[0] += av.x; G4[1] += av.y; G4[2] += av.z; G4[3] += av.w;
-                }
-                comb_stamp(l, 3);
-                const float inv = 1.0f / gl[h];
-                if (ok) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) ll_store(out + h * D + 4 * lane + i, ll_word(G4[i] * inv, tag));
-                }
-                comb_stamp(l, 4);
-            }
+            for (int i = 0; i < 4; ++i) acc[(warp * 2 + hh) * D + 4 * lane + i] = am[hh][i];
+            if (lane == 0) { ml[warp * 4 + 2 * hh] = mm[hh]; ml[warp * 4 + 2 * hh + 1] = lsum[hh]; }
         }
     }
 
