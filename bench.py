@@ -33,6 +33,14 @@ WEIGHT_BYTES = 1_192_101_888            # 28 layers + lm_head + norms + one embe
 KV_BYTES_PER_POS = 114_688              # K+V, all layers, one position (bf16)
 
 
+# DRAM bytes (read + write) of one decode_step_kernel launch at position ~20 from
+# one `ncu --set full` capture (profiles/decode_step_kernel_config2.md).  DRAM
+# traffic tracks the algorithmic bytes (the same holds at p = 8192,
+# profiles/decode_step_kernel_p8192.md), so the bench scales it to its own mean
+# position by the algorithmic-bytes ratio.
+NCU_TRAFFIC_P20 = 1_194_463_000 + 3_732_736
+
+
 def bytes_per_token(pos: int) -> int:
     """Algorithmic HBM bytes of one decode token at position ``pos``: every
     weight once, K/V rows 0..pos read, row pos written."""
@@ -406,7 +414,9 @@ def run_ours(args, rank, world, local):
                        "l2": "no flush: weights 1.19 GB streamed per token > 126 MB L2"},
             "gpu_launches": args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": None,
+                         "frac": round(achieved / hbm, 4),
+                         "traffic": round(NCU_TRAFFIC_P20 * bytes_per_token(p_mid) / bytes_per_token(20)),
+                         "traffic_source": "ncu capture at p~20, scaled by algorithmic bytes",
                          "peak_kind": hbm_kind, "bytes_per_launch": bytes_per_token(p_mid),
                          "launch_ms": round(launch_ms, 5)},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 32},
