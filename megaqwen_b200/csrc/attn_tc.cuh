@@ -105,8 +105,11 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
 
     const int S = args.S;
     const int nqb = (S + BQ - 1) / BQ;
-    const int qb = nqb - 1 - (int)blockIdx.x;   // heavier (later) query blocks first
-    const int h = blockIdx.y, b = blockIdx.z, kvh = h >> 1;
+    // grid (heads, batch, query blocks): CTAs are dispatched in linear block
+    // order, so every (head, sequence) pair's heaviest (latest) query block
+    // starts before any lighter one (longest-processing-time-first).
+    const int qb = nqb - 1 - (int)blockIdx.z;
+    const int h = blockIdx.x, b = blockIdx.y, kvh = h >> 1;
     const int q0 = qb * BQ;
     const int nt = qb + 1;                      // key tiles 0..qb (causal)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -303,6 +303,17 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
         int i = 0;
         for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++i) {
             const int b = i & 1, u = i >> 1;
+            if (EPI == EPI_ADD_F32) {
+                // the residual rows this lane adds to: pull them into L2 while the MMAs run
+                const int prow = (t / args.tiles_n) * GEMM_BM + quad * 32 + lane;
+                if (prow < args.M) {
+                    const float* pp = reinterpret_cast<const float*>(args.C) + (size_t)prow * args.ldc +
+                                      (t % args.tiles_n) * BN + half * HB;
+#pragma unroll
+                    for (int q = 0; q < HB * 4; q += 128)
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(pp) + q));
+                }
+            }
             if (!bounded_wait(&accf[b], u & 1, args.timeout_cycles) || *abort_flag) {
                 if (lane == 0) atomicExch(args.err, 34);
                 *abort_flag = 1;

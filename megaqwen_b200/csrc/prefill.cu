@@ -277,7 +277,7 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
                     fa_args.trace = g_fa_trace;
                 }
             }
-            dim3 fgrid((S + fa::BQ - 1) / fa::BQ, MQ_NUM_Q_HEADS, B);
+            dim3 fgrid(MQ_NUM_Q_HEADS, B, (S + fa::BQ - 1) / fa::BQ);
             fa::fa_tc_kernel<<<fgrid, fa::THREADS, fa::SMEM, st>>>(tmQ, tmK, tmV, fa_args);
         }
         MQ_TRY(gemm_bf16(Ob, 2048, W.o_proj_weight, 2048, nullptr, X, 1024, M, 1024, 2048, EPI_ADD_F32, err, st));
