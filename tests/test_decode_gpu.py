@@ -106,8 +106,9 @@ def test_decode_steps_match_oracle_small(num_layers):
 
 
 def test_split_k_attention_matches_oracle():
-    """Small attention chunks force several work units per kv head and the
-    last-arriver combine, at positions where one unit would also do."""
+    """Small attention chunks force several work units per kv head (up to 18,
+    so the combiner's warps poll more than one unit each) and the fixed
+    combiner's merge, at positions where one unit would also do."""
     dec = make_decoder(2, 512)
     o = make_oracle(2, 512)
     dec.set_attn_chunk(8)
