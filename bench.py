@@ -419,7 +419,8 @@ def run_ours(args, rank, world, local):
                          "traffic_source": "ncu capture at p~20, scaled by algorithmic bytes",
                          "peak_kind": hbm_kind, "bytes_per_launch": bytes_per_token(p_mid),
                          "launch_ms": round(launch_ms, 5)},
-            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 32},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 16,
+                    "d2h_path": "token, error, info, seq written by the kernel to mapped pinned host memory"},
             "clocks": clk.summary(),
             "positions": sweep,
             "prefill": sweep_prefill,

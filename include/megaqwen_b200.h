@@ -97,6 +97,15 @@ void launch_ldg_decode_with_logits(int input_token_id, int* output_token_id, flo
                                    void* block_max_vals, void* block_max_idxs, int num_layers, int position,
                                    int cache_len, int max_seq_len, float attn_scale, cudaStream_t stream);
 
+/* Result of a decode step written straight to host memory (see
+ * mq_decode_params.host_result).  seq is written last. */
+typedef struct mq_host_result {
+    volatile unsigned int seq;
+    int token;
+    unsigned int error;
+    unsigned int info;
+} mq_host_result;
+
 /* ---- native API ------------------------------------------------------------
  * The decode step with an explicit, caller-owned workspace and an explicit
  * status.  Extends launch_ldg_decode (fused_decode_ldg.cu:893-921) with:
@@ -136,6 +145,14 @@ typedef struct mq_decode_params {
                                       stamps per CTA, phase and tile (profiling); NULL: off.
                                       Only kernel start/end are stamped unless the library was
                                       built with MQ_DECODE_TRACE=1 (see megaqwen_b200/build.py) */
+    mq_host_result* host_result;   /* optional: device-visible address of mapped pinned host memory
+                                      (cudaHostAllocMapped + cudaHostGetDevicePointer).  The step's
+                                      last CTA writes token, error and info there, then seq =
+                                      host_seq, so a host thread can wait for the token without a
+                                      device-to-host copy and a stream synchronise.  Nothing is
+                                      written when the step fails before its argmax: wait with a
+                                      bound and fall back to mq_decode_fetch.  NULL: off */
+    unsigned int host_seq;
 } mq_decode_params;
 
 size_t mq_decode_workspace_bytes(void);

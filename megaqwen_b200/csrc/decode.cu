@@ -169,6 +169,8 @@ struct KParams {
     long long timeout_ns;
     int inject_skip_cta;
     unsigned long long* trace;
+    mq_host_result* host_result;   // mapped host memory (device-visible address) or null
+    uint32_t host_seq;
 };
 static_assert(sizeof(KParams) <= 256 && sizeof(KParams) % 4 == 0, "KParams copy fits its slot");
 
@@ -1241,6 +1243,16 @@ struct Consumer {
                 int tok = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
                 atomicExch(&C->lm_count, 0u);
                 if (P.output_token) *P.output_token = tok;
+                if (P.host_result) {
+                    // token, error, info first, then the sequence word the host waits on
+                    volatile mq_host_result* hr = P.host_result;
+                    hr->token = tok;
+                    hr->error = ld_relaxed_u32(&C->error);
+                    hr->info = C->info;
+                    __threadfence_system();
+                    hr->seq = P.host_seq;
+                    __threadfence_system();
+                }
                 C->last_token = tok;
                 C->last_position = S.pos;
                 if (P.position_ptr) *P.position_ptr = S.pos + 1;
@@ -1479,6 +1491,8 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     k.timeout_ns = p->timeout_ns > 0 ? p->timeout_ns : 2000000000ll;
     k.inject_skip_cta = p->inject_skip_cta;
     k.trace = p->trace;
+    k.host_result = p->host_result;
+    k.host_seq = p->host_seq;
 
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(G);

@@ -16,7 +16,9 @@
 #include <c10/cuda/CUDAStream.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
+#include <cstring>
 #include <stdexcept>
 #include <string>
 #include <tuple>
@@ -137,7 +139,9 @@ public:
         attn_scale_ = 1.0f / sqrtf(128.0f);
     }
 
-    virtual ~MegakernelDecoder() = default;
+    virtual ~MegakernelDecoder() {
+        if (hres_) cudaFreeHost(hres_);   // errors at interpreter exit are ignored
+    }
 
     int decode_step(int input_token_id) {
         step(input_token_id, nullptr, nullptr);
@@ -270,10 +274,60 @@ protected:
         cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
         mq_decode_params p = params(input_token_id, logits);
         p.input_token_ptr = token_ptr;
+        const bool fast = ensure_host_result();
+        if (fast) {
+            if (++hseq_ == 0) ++hseq_;
+            p.host_result = hres_dev_;
+            p.host_seq = hseq_;
+        }
         int rc = mq_decode(&p, stream);
         if (rc) raise_engine(rc, 0, "decode_step");
-        check_device("decode_step", stream);
+        if (fast && wait_host_result(hseq_, stream)) last_token_ = hres_->token;
+        else check_device("decode_step", stream);
         position_ += 1;
+    }
+
+    // Mapped pinned host memory the kernel writes its result to (one per
+    // decoder).  Without it every step would pay a device-to-host copy and a
+    // stream synchronise.
+    bool ensure_host_result() {
+        if (hres_) return true;
+        if (hres_failed_) return false;
+        void* h = nullptr;
+        void* d = nullptr;
+        if (cudaHostAlloc(&h, sizeof(mq_host_result), cudaHostAllocMapped | cudaHostAllocPortable) != cudaSuccess ||
+            cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+            if (h) cudaFreeHost(h);
+            cudaGetLastError();
+            hres_failed_ = true;
+            return false;
+        }
+        std::memset(h, 0, sizeof(mq_host_result));
+        hres_ = static_cast<mq_host_result*>(h);
+        hres_dev_ = static_cast<mq_host_result*>(d);
+        return true;
+    }
+
+    // Spin until the step's sequence word arrives.  Returns false (the caller
+    // then takes the copy-and-synchronise path, which reports errors) when the
+    // step recorded an error or the stream finished without writing it.
+    bool wait_host_result(unsigned int want, cudaStream_t stream) {
+        for (unsigned int i = 1;; ++i) {
+            if (hres_->seq == want) {
+                std::atomic_thread_fence(std::memory_order_acquire);
+                return hres_->error == 0;
+            }
+            if ((i & 1023u) == 0) {
+                const cudaError_t q = cudaStreamQuery(stream);
+                if (q != cudaErrorNotReady) {
+                    if (hres_->seq == want) {
+                        std::atomic_thread_fence(std::memory_order_acquire);
+                        return hres_->error == 0;
+                    }
+                    return false;
+                }
+            }
+        }
     }
 
     int num_layers_;
@@ -286,6 +340,10 @@ protected:
     long long timeout_ns_ = 0;
     int inject_skip_cta_ = 0;
     unsigned long long* trace_ = nullptr;
+    mq_host_result* hres_ = nullptr;       // host address of the mapped result
+    mq_host_result* hres_dev_ = nullptr;   // its device-visible address
+    bool hres_failed_ = false;
+    unsigned int hseq_ = 0;
     torch::Device device_{torch::kCUDA, 0};
     torch::Tensor embed_, final_norm_, lm_head_, cos_, sin_, d_layers_;
     std::vector<torch::Tensor> layer_tensors_;

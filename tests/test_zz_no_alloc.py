@@ -36,7 +36,8 @@ class DecodeParams(ctypes.Structure):
         ("workspace_bytes", ctypes.c_size_t), ("num_layers", ctypes.c_int), ("position", ctypes.c_int),
         ("position_ptr", ctypes.c_void_p), ("max_seq_len", ctypes.c_int), ("attn_scale", ctypes.c_float),
         ("num_ctas", ctypes.c_int), ("attn_chunk", ctypes.c_int), ("timeout_ns", ctypes.c_longlong),
-        ("inject_skip_cta", ctypes.c_int), ("trace", ctypes.c_void_p),
+        ("inject_skip_cta", ctypes.c_int), ("trace", ctypes.c_void_p), ("host_result", ctypes.c_void_p),
+        ("host_seq", ctypes.c_uint),
     ]
 
 
