@@ -27,7 +27,7 @@ def _cache_rel_err(dev_cache, ref_cache, upto):
     return ((got - ref).abs().max() / ref.abs().max().clamp_min(1e-6)).item()
 
 
-@pytest.mark.parametrize("num_layers,S", [(2, 200), (1, 2048), (28, 64)])
+@pytest.mark.parametrize("num_layers,S", [(2, 1), (2, 8), (2, 200), (1, 2048), (28, 64)])
 def test_prefill_matches_oracle(num_layers, S):
     from megaqwen_b200.weights import seeded_prompt
     ids = seeded_prompt(S, seed=5)
