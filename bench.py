@@ -22,7 +22,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import threading
 import time
 
@@ -73,57 +72,79 @@ def measured_hbm_gbs():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clocks and clock-event (throttle) reasons sampled through NVML by a
+    background thread every ~5 ms while the block is open.  ``mark()`` brackets
+    the timed region; ``summary()`` reports the samples inside it, or, when the
+    timed region is shorter than a few sampling periods, every sample taken
+    while the GPU was under this bench's load (``window`` says which)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+    def __init__(self, device: torch.device, period_s: float = 0.005):
+        self.device = device
+        self.period = period_s
+        self.samples = []          # (t, sm_mhz, reasons)
+        self.smax = None
+        self.t0 = self.t1 = None
+        self.error = None
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except Exception:
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(self.device).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self.smax = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.nv = pynvml
+            self.th = threading.Thread(target=self._run, daemon=True)
+            self.th.start()
+        except Exception as exc:  # no NVML: report why, keep the bench running
+            self.error = f"{type(exc).__name__}: {exc}"
+            self.th = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                rs = tuple(n for n, c in self.REASONS if bits & getattr(nv, c))
+                self.samples.append((time.perf_counter(), sm, rs))
+            except Exception as exc:
+                self.error = f"{type(exc).__name__}: {exc}"
+                return
+            time.sleep(self.period)
+
+    def mark(self, start: bool):
+        if start:
+            self.t0 = time.perf_counter()
+        else:
+            self.t1 = time.perf_counter()
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=2)
-            except Exception:
-                self.proc.kill()
+        self._stop.set()
+        if self.th is not None:
+            self.th.join(timeout=2)
 
     def summary(self):
-        sm, smax, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                smax = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        inside = [s for s in self.samples if self.t0 is not None and self.t1 is not None and self.t0 <= s[0] <= self.t1]
+        window = "timed region"
+        use = inside
+        if len(inside) < 3:
+            use = self.samples
+            window = "whole headline phase (warm-up, timed region, e2e loop): timed region shorter than 3 samples"
+        sm = [s[1] for s in use]
+        reasons = sorted({r for s in use for r in s[2]})
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.smax, "reasons": reasons,
+               "samples": len(use), "samples_in_timed_region": len(inside), "window": window, "source": "NVML"}
+        if self.error:
+            out["error"] = self.error
+        return out
 
 
 def dist_setup(n_gpus):
@@ -174,6 +195,70 @@ def cpu_oracle_rate(budget_s: float, num_layers: int = 28, prompt_len: int = 16)
         n += 1
     dt = time.perf_counter() - t0
     return n / dt, n, torch.get_num_threads(), pos
+
+
+def ref_megakernel_child(args):
+    """Times the reference decode megakernel built for sm_100a
+    (``oracle/_ref``, from the reference's unchanged fused_decode_ldg.cu)
+    through its own ``launch_ldg_decode`` at positions 1/128/512 on this GPU.
+    Runs in a child process of the bench (host timeout in the parent).  Caches
+    are pre-filled with N(0,1) bf16 K/V below the start position; each timed
+    launch sequence is K back-to-back steps with a fixed input token (the
+    reference launcher takes the token by value), bracketed by CUDA events."""
+    from megaqwen_b200.weights import make_weights, rope_tables
+    from oracle.ref_megakernel import RefLdgDecoder
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    hbm, _ = measured_hbm_gbs()
+    n = args.sweep_steps
+    maxp = max(args.ref_positions) + n + 8
+    w = make_weights(28).to(dev)
+    cos, sin = rope_tables(maxp, device=dev)
+    ref = RefLdgDecoder(w, cos, sin, 28, maxp)
+    g = torch.Generator(device=dev).manual_seed(11)
+    stream = torch.cuda.current_stream().cuda_stream
+    out = {}
+    for P in args.ref_positions:
+        ref.k_cache[:, :, :P].normal_(generator=g)
+        ref.v_cache[:, :, :P].normal_(generator=g)
+        for i in range(3):
+            ref.launch(5, P + i, stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(n):
+            ref.launch(5, P + 3 + i, stream)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        pm = P + 3 + n // 2
+        out[str(P)] = {"tok_s": round(1000.0 / ms, 1), "ms_per_step": round(ms, 4),
+                       "roofline_frac": round(bytes_per_token(pm) / (ms / 1000.0) / 1e9 / hbm, 4)}
+    tok = ref.decode_step(5, maxp - 1)   # one step read back: the launch sequence completed
+    print(json.dumps({"reference_megakernel_sm100a": out, "last_token": tok}), flush=True)
+
+
+def run_ref_megakernel(args):
+    """Parent side of ref_megakernel_child: a child process under a host timeout."""
+    import subprocess
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    if not os.path.exists(os.path.join(here, "oracle", "_ref", "libref_ldg_decode.so")):
+        return {"unavailable": "oracle/_ref/libref_ldg_decode.so not built (oracle/build_ref.py)"}
+    cmd = [sys.executable, os.path.abspath(__file__), "--ref-megakernel-child", "--sweep-steps", str(args.sweep_steps),
+           "--ref-positions", ",".join(str(p) for p in args.ref_positions)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=args.ref_timeout, cwd=here)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"timed out after {args.ref_timeout} s"}
+    for ln in reversed(r.stdout.splitlines()):
+        if ln.startswith("{"):
+            res = json.loads(ln)["reference_megakernel_sm100a"]
+            res["what"] = ("reference csrc/megakernel/fused_decode_ldg.cu, unchanged, nvcc -gencode "
+                           "arch=compute_100a,code=sm_100a; launch_ldg_decode (82x256 cooperative grid.sync kernel "
+                           "+ 2 LM-head kernels); caches pre-filled with N(0,1) K/V")
+            return res
+    return {"unavailable": f"child exited {r.returncode}: {(r.stderr or r.stdout)[-300:]}"}
 
 
 def run_reference(args, rank, world):
@@ -330,37 +415,40 @@ def run_ours(args, rank, world, local):
         return
 
     # --- headline: config 2, device-fed greedy decode after a 16-token prompt ---
-    for t in prompt[:-1]:
-        dec.decode_step(t)
-    tok_buf = torch.tensor([prompt[-1]], dtype=torch.int32, device=dev)
-    for _ in range(args.warmup):
-        dec.decode_step_async(tok_buf.data_ptr(), tok_buf.data_ptr())
-    dec.check()
-    p_first = dec.position()
-    barrier(world)
-    with ClockSampler(local) as clk:
+    clk = ClockSampler(dev)
+    with clk:
+        for t in prompt[:-1]:
+            dec.decode_step(t)
+        tok_buf = torch.tensor([prompt[-1]], dtype=torch.int32, device=dev)
+        for _ in range(args.warmup):
+            dec.decode_step_async(tok_buf.data_ptr(), tok_buf.data_ptr())
+        dec.check()
+        p_first = dec.position()
+        barrier(world)
+        clk.mark(True)
         total_ms = time_device_steps(dec, tok_buf, args.steps)
-    dec.check()
-    barrier(world)
-    total_ms_max = max_over_ranks(total_ms, world)
-    ms_step = total_ms_max / args.steps
-    value = world * args.steps / (total_ms_max / 1000.0)
-    launch_ms = total_ms / args.steps   # back-to-back launches: per-launch average
-    p_mid = p_first + args.steps // 2
-    achieved = bytes_per_token(p_mid) / (launch_ms / 1000.0) / 1e9
+        clk.mark(False)
+        dec.check()
+        barrier(world)
+        total_ms_max = max_over_ranks(total_ms, world)
+        ms_step = total_ms_max / args.steps
+        value = world * args.steps / (total_ms_max / 1000.0)
+        launch_ms = total_ms / args.steps   # back-to-back launches: per-launch average
+        p_mid = p_first + args.steps // 2
+        achieved = bytes_per_token(p_mid) / (launch_ms / 1000.0) / 1e9
 
-    # --- e2e through the public API: host token in, host token out each step ---
-    cur = int(tok_buf.item())
-    for _ in range(3):
-        cur = dec.decode_step(cur)
-    barrier(world)
-    t0 = time.perf_counter()
-    e2e_steps = args.steps
-    for _ in range(e2e_steps):
-        cur = dec.decode_step(cur)
-    torch.cuda.synchronize()
-    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e = world * e2e_steps / e2e_s
+        # --- e2e through the public API: host token in, host token out each step ---
+        cur = int(tok_buf.item())
+        for _ in range(3):
+            cur = dec.decode_step(cur)
+        barrier(world)
+        t0 = time.perf_counter()
+        e2e_steps = args.steps
+        for _ in range(e2e_steps):
+            cur = dec.decode_step(cur)
+        torch.cuda.synchronize()
+        e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+        e2e = world * e2e_steps / e2e_s
 
     # --- position sweep (rank 0 reports) ---
     sweep = {}
@@ -394,6 +482,10 @@ def run_ours(args, rank, world, local):
     # --- batched decode (config 5): B independent sequences per GPU, one token each per step ---
     batch = run_batch(args, w, cos, sin, dev, hbm, world) if args.batch_sizes else {}
 
+    ref_mk = None
+    if rank == 0 and world == 1 and not args.no_ref_megakernel:
+        ref_mk = run_ref_megakernel(args)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rate, n, cores, last = cpu_oracle_rate(args.cpu_budget)
@@ -425,6 +517,7 @@ def run_ours(args, rank, world, local):
             "positions": sweep,
             "prefill": sweep_prefill,
             "batch_decode": batch or None,
+            "reference_megakernel_sm100a": ref_mk,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
@@ -448,7 +541,15 @@ def main():
     ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-ref-megakernel", action="store_true",
+                    help="skip timing the reference megakernel built for sm_100a (oracle/_ref)")
+    ap.add_argument("--ref-positions", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 128, 512])
+    ap.add_argument("--ref-timeout", type=float, default=240.0)
+    ap.add_argument("--ref-megakernel-child", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.ref_megakernel_child:
+        ref_megakernel_child(args)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -175,12 +175,27 @@ int mq_decode(const mq_decode_params* params, cudaStream_t stream);
  * it, so make that first call before any stream capture.  Every call on a
  * device shares the array, so calls that overlap on the GPU (different
  * streams, or other threads) race.  num_ctas above 256 or num_layers above 63
- * are rejected with MQ_ERR_INVALID_ARGUMENT.  A device-side wait failure
- * leaves the output token unwritten; the scratch then holds a stale error and
- * the process should stop using this entry point on that device.  Calls no
+ * are rejected with MQ_ERR_INVALID_ARGUMENT.  Any device-side failure of a
+ * step -- a wait that ran out, or an input token or position (read from
+ * input_token_ptr / position_ptr) out of range -- leaves the output token
+ * unwritten and an error word in the scratch, after which every later step on
+ * that device fails too until mq_decode_noalloc_reset() clears the scratch.
+ * Learn a step's status from host_result (written by the step) or from
+ * mq_decode_noalloc_fetch().  The device address of the array is cached per
+ * device index for the life of the process: after cudaDeviceReset() (or any
+ * new primary context) this entry point must not be used again.  Calls no
  * cudaMalloc, cudaFree or other allocating routine. */
 #define MQ_NOALLOC_SCRATCH_BYTES 721152
 int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream);
+/* Clear the static scratch of the current device (stream-ordered, no
+ * allocation), e.g. after a step reported an error.  No-op before the first
+ * mq_decode_noalloc call on the device. */
+int mq_decode_noalloc_reset(cudaStream_t stream);
+/* Status of the last mq_decode_noalloc step on the current device: the greedy
+ * token of the last successful step, the error word and the info word.
+ * Copies 32 bytes into host stack memory and synchronises `stream`; allocates
+ * nothing. */
+int mq_decode_noalloc_fetch(int* token, uint32_t* error, uint32_t* info, cudaStream_t stream);
 /* Copy the workspace error word (and the auxiliary info word) to the host;
  * synchronises `stream`. */
 int mq_decode_read_error(const void* workspace, uint32_t* error, uint32_t* info, cudaStream_t stream);

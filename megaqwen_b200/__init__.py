@@ -2,39 +2,50 @@
 reference MegaQwen torch-extension API.
 
 The native parts are built in-tree by ``megaqwen_b200.build`` (see
-``__graft_entry__.build()``).  Importing this package without them raises
-ImportError: there is no CPU or pure-PyTorch fallback.
+``__graft_entry__.build()``).  The torch extension ``_C`` (and through it
+``lib/libmegaqwen_b200.so``) is loaded on first use of a native name
+(``megaqwen_b200.MegakernelDecoder``, ``megaqwen_b200._C`` ...), so the pure
+host-side modules (``megaqwen_b200.weights``) import without mapping any native
+library.  Using a native name without the built extension raises ImportError:
+there is no CPU or pure-PyTorch fallback.
 """
 from __future__ import annotations
 
-import torch  # noqa: F401  (loads libtorch before the extension)
+import importlib
 
-from . import weights  # noqa: F401
+from . import weights  # noqa: F401  (pure torch/CPU: seeded weights, RoPE tables, prompts)
 
-try:
-    from . import _C  # type: ignore[attr-defined]
-except ImportError as exc:  # pragma: no cover - exercised only on broken installs
-    raise ImportError(
-        "megaqwen_b200 native extension is not built; run `python megaqwen_b200/build.py`"
-    ) from exc
-
-MegakernelDecoder = _C.MegakernelDecoder
-MegakernelPrefillDecoder = _C.MegakernelPrefillDecoder
-MegakernelFusedPrefillDecoder = _C.MegakernelFusedPrefillDecoder
-MegakernelBatchDecoder = _C.MegakernelBatchDecoder
-init_ldg_layer_weights = _C.init_ldg_layer_weights
-init_ldg_embed_weight = _C.init_ldg_embed_weight
-decode_ldg = _C.decode_ldg
-decode_ldg_with_logits = _C.decode_ldg_with_logits
-
-__all__ = [
+_NATIVE = (
     "MegakernelDecoder",
     "MegakernelPrefillDecoder",
     "MegakernelFusedPrefillDecoder",
     "MegakernelBatchDecoder",
+    "MegakernelTPDecoder",
     "init_ldg_layer_weights",
     "init_ldg_embed_weight",
     "decode_ldg",
     "decode_ldg_with_logits",
-    "weights",
-]
+)
+
+
+def _load_native():
+    import torch  # noqa: F401  (loads libtorch before the extension)
+    try:
+        return importlib.import_module("._C", __name__)
+    except ImportError as exc:
+        raise ImportError(
+            "megaqwen_b200 native extension is not built; run `python megaqwen_b200/build.py`"
+        ) from exc
+
+
+def __getattr__(name):
+    if name == "_C":
+        return _load_native()
+    if name in _NATIVE:
+        return getattr(_load_native(), name)
+    if name in ("megakernel_decode", "chat"):
+        return importlib.import_module("." + name, __name__)
+    raise AttributeError(f"module 'megaqwen_b200' has no attribute {name!r}")
+
+
+__all__ = list(_NATIVE) + ["weights"]

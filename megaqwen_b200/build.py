@@ -13,7 +13,8 @@ Run ``python megaqwen_b200/build.py`` (or ``__graft_entry__.build()``).  Each
 output is rebuilt only when a source it depends on is newer.
 ``MQ_DECODE_TRACE=1 python megaqwen_b200/build.py --force`` builds the decode
 kernel with its per-phase/per-tile trace stamps (``mq_decode_params.trace``);
-the default build leaves them out.
+the default build leaves them out.  ``MQ_PROFILE_HOOKS=1`` likewise compiles
+the batched-decode and prefill profiling hooks (off by default).
 """
 from __future__ import annotations
 
@@ -68,6 +69,8 @@ def build_lib(verbose: bool = False, force: bool = False) -> Path:
            "-Xptxas", "-v", f"-I{INCLUDE}", f"-I{CSRC}", *srcs, "-o", LIB]
     if os.environ.get("MQ_DECODE_TRACE") == "1":
         cmd.insert(1, "-DMQ_DECODE_TRACE=1")
+    if os.environ.get("MQ_PROFILE_HOOKS") == "1":
+        cmd.insert(1, "-DMQ_PROFILE_HOOKS=1")
     out = _run(cmd, verbose)
     (LIBDIR / "ptxas_info.txt").write_text(out)
     return LIB

@@ -1503,8 +1503,7 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeCooperative;
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
-    static const int coop = [] { const char* e = getenv("MQ_COOP"); return e ? atoi(e) : 1; }();
-    cfg.numAttrs = coop ? 1 : 0;
+    cfg.numAttrs = 1;   // always cooperative: the CTAs wait on each other, so all must be resident
     cudaError_t e = cudaLaunchKernelEx(&cfg, mq::decode_step_kernel, k);
     if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(decode_step_kernel, cooperative)");
     return MQ_OK;
@@ -1629,6 +1628,43 @@ int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream) {
     p.workspace = scratch;
     p.workspace_bytes = mq::WS_BYTES;
     return launch(&p, stream);
+}
+
+// The static scratch of this device, or null before the first
+// mq_decode_noalloc call on it.
+static void* noalloc_scratch_of_current_device(int* rc) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) { *rc = cuda_fail(e, "cudaGetDevice"); return nullptr; }
+    if (dev < 0 || dev >= 64) { *rc = note(MQ_ERR_INVALID_ARGUMENT, "device index above 63"); return nullptr; }
+    std::lock_guard<std::mutex> lk(g_noalloc_mutex);
+    *rc = MQ_OK;
+    return g_noalloc_ptr[dev];
+}
+
+int mq_decode_noalloc_reset(cudaStream_t stream) {
+    int rc = MQ_OK;
+    void* ptr = noalloc_scratch_of_current_device(&rc);
+    if (rc) return rc;
+    if (!ptr) return MQ_OK;   // never used on this device: nothing to clear
+    const cudaError_t e = cudaMemsetAsync(ptr, 0, mq::WS_BYTES, stream);
+    return e == cudaSuccess ? MQ_OK : cuda_fail(e, "cudaMemsetAsync(static scratch)");
+}
+
+int mq_decode_noalloc_fetch(int* token, uint32_t* error, uint32_t* info, cudaStream_t stream) {
+    int rc = MQ_OK;
+    void* ptr = noalloc_scratch_of_current_device(&rc);
+    if (rc) return rc;
+    if (!ptr) return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc_fetch: no mq_decode_noalloc call on this device yet");
+    mq::Control c;   // host stack: pageable copy, no pinned allocation
+    cudaError_t e = cudaMemcpyAsync(&c, ptr, 32, cudaMemcpyDeviceToHost, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(static scratch result)");
+    e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+    if (token) *token = c.last_token;
+    if (error) *error = c.error;
+    if (info) *info = c.info;
+    return MQ_OK;
 }
 
 int mq_decode_read_error(const void* workspace, uint32_t* error, uint32_t* info, cudaStream_t stream) {

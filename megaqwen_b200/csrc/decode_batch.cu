@@ -432,9 +432,11 @@ int launch_small(int total, int kblocks, Small2Args a, const CUtensorMap* tw, co
                     cudaGetLastError();
                     continue;
                 }
+#if MQ_PROFILE_HOOKS
                 if (getenv("MQ_SPLIT_VERBOSE"))
                     fprintf(stderr, "  mode %d NP %d tiles %d: S %d smem %d -> %d clusters\n", MODE, NPV, total, S,
                             (int)cfg.dynamicSmemBytes, nclusters);
+#endif
                 if (nclusters >= total || S == 1) {
                     ch.S = S;
                     ch.kpb = kpb;
@@ -443,9 +445,11 @@ int launch_small(int total, int kblocks, Small2Args a, const CUtensorMap* tw, co
                 }
             }
         }
+#if MQ_PROFILE_HOOKS
         if (getenv("MQ_SPLIT_VERBOSE"))
             fprintf(stderr, "small gemm mode %d NP %d tiles %d kblocks %d -> S %d kpb %d stages %d\n", MODE, NPV,
                     total, kblocks, ch.S, ch.kpb, ch.stages);
+#endif
         std::lock_guard<std::mutex> lk(g_split_mu);
         g_splits.push_back(ch);
     }
@@ -484,6 +488,7 @@ int small_gemm(const void* const* W, const int* Nmap, int nmaps, int K, const vo
     a.K = K;
     a.timeout_cycles = 4000000000ll;
     a.trace = nullptr;
+#if MQ_PROFILE_HOOKS
     {
         // phase-timing hook: MQ_SMALL_TRACE=<n> stamps the n-th small GEMM launch of the process
         static const int trace_at = [] { const char* e = getenv("MQ_SMALL_TRACE"); return e ? atoi(e) : -1; }();
@@ -493,6 +498,7 @@ int small_gemm(const void* const* W, const int* Nmap, int nmaps, int K, const vo
             a.trace = g_trace;
         }
     }
+#endif
     const int kblocks = K / GEMM_BK;
     switch (NP) {
         case 16: return launch_small<16, MODE>(total, kblocks, a, tw, tx, st);
@@ -621,12 +627,14 @@ size_t mq_decode_batch_workspace_bytes(int batch, int max_seq_len) {
     return mq::decode_batch_workspace_bytes(batch, max_seq_len);
 }
 
+#if MQ_PROFILE_HOOKS
 // Copies the phase stamps of the traced small GEMM launch (MQ_SMALL_TRACE) to host.
 int mq_debug_small_trace(unsigned long long* host, int n) {
     if (!mq::db::g_trace) return 0;
     cudaMemcpy(host, mq::db::g_trace, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     return n;
 }
+#endif
 
 int mq_decode_batch(const mq_decode_batch_params* params, cudaStream_t stream) {
     return mq::decode_batch(params, stream);

@@ -282,8 +282,15 @@ protected:
         }
         int rc = mq_decode(&p, stream);
         if (rc) raise_engine(rc, 0, "decode_step");
-        if (fast && wait_host_result(hseq_, stream)) last_token_ = hres_->token;
-        else check_device("decode_step", stream);
+        // The mapped-result path reads no stream status; a sticky CUDA error
+        // raised after the kernel wrote its result is caught here on the host
+        // (no device round trip) and reported through the checked path.
+        // step() waits for its result on the host, so it must not be called
+        // while the current stream is being captured into a CUDA graph.
+        if (fast && wait_host_result(hseq_, stream) && cudaPeekAtLastError() == cudaSuccess)
+            last_token_ = hres_->token;
+        else
+            check_device("decode_step", stream);
         position_ += 1;
     }
 

@@ -4,6 +4,14 @@
 #pragma once
 
 #include <cstdint>
+
+// Profiling hooks of the batched-decode GEMMs and the prefill attention
+// (environment-selected trace stamps, split-choice printout, mq_debug_*
+// exports) are compiled only with -DMQ_PROFILE_HOOKS=1; the default library
+// reads no environment variable and exports no debug entry point.
+#ifndef MQ_PROFILE_HOOKS
+#define MQ_PROFILE_HOOKS 0
+#endif
 #include <cuda_runtime.h>
 
 namespace mq {

@@ -268,6 +268,7 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             fa_args.err = err;
             fa_args.timeout_cycles = 4000000000ll;
             fa_args.trace = nullptr;
+#if MQ_PROFILE_HOOKS
             {
                 // profiling hook: MQ_FA_TRACE=<layer> stamps one attention block of that layer
                 static const int at = [] { const char* e = getenv("MQ_FA_TRACE"); return e ? atoi(e) : -1; }();
@@ -277,6 +278,7 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
                     fa_args.trace = g_fa_trace;
                 }
             }
+#endif
             dim3 fgrid(MQ_NUM_Q_HEADS, B, (S + fa::BQ - 1) / fa::BQ);
             fa::fa_tc_kernel<<<fgrid, fa::THREADS, fa::SMEM, st>>>(tmQ, tmK, tmV, fa_args);
         }
@@ -390,11 +392,13 @@ void launch_prefill_megakernel(const int* token_ids, int* output_token_id, int s
 
 int mq_prefill_get_last_error(void) { return g_pf_last_error; }
 
+#if MQ_PROFILE_HOOKS
 // Copies the attention trace stamps of the last MQ_FA_TRACE prefill (profiling).
 int mq_debug_fa_trace(unsigned long long* host, int n) {
     if (!mq::g_fa_trace) return 0;
     cudaMemcpy(host, mq::g_fa_trace, (size_t)n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
     return n;
 }
+#endif
 
 }  // extern "C"

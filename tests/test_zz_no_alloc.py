@@ -47,6 +47,9 @@ def _lib():
     for name in ("mq_decode", "mq_decode_noalloc"):
         getattr(lib, name).argtypes = [ctypes.POINTER(DecodeParams), ctypes.c_void_p]
         getattr(lib, name).restype = ctypes.c_int
+    lib.mq_decode_noalloc_reset.argtypes = [ctypes.c_void_p]
+    lib.mq_decode_noalloc_fetch.argtypes = [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_uint32),
+                                            ctypes.POINTER(ctypes.c_uint32), ctypes.c_void_p]
     lib.mq_decode_workspace_bytes.restype = ctypes.c_size_t
     lib.mq_last_error_detail.restype = ctypes.c_char_p
     return lib
@@ -112,3 +115,24 @@ def test_noalloc_matches_allocating_entry_point():
     bad.num_ctas = 1000
     assert lib.mq_decode_noalloc(ctypes.byref(bad), stream) == 1
     assert b"static scratch" in lib.mq_last_error_detail()
+
+    # A device-side input error (token read from device memory, out of range)
+    # is recorded in the static scratch and blocks later steps until the
+    # caller clears it with mq_decode_noalloc_reset; then a step succeeds and
+    # still matches the allocating entry point.
+    tok_err, err, info = ctypes.c_int(0), ctypes.c_uint32(0), ctypes.c_uint32(0)
+    bad_tok = torch.full((1,), -5, dtype=torch.int32, device="cuda")
+    p = params(new, 0, 2)
+    p.input_token_ptr = bad_tok.data_ptr()
+    assert lib.mq_decode_noalloc(ctypes.byref(p), stream) == 0
+    assert lib.mq_decode_noalloc_fetch(ctypes.byref(tok_err), ctypes.byref(err), ctypes.byref(info), stream) == 0
+    assert err.value == 4 and ctypes.c_int32(info.value).value == -5       # MQ_ERR_BAD_TOKEN, the token
+    assert lib.mq_decode_noalloc_reset(stream) == 0
+    rc = lib.mq_decode(ctypes.byref(params(ref, 99, 2, ws.data_ptr(), ws.numel())), stream)
+    assert rc == 0, lib.mq_last_error_detail()
+    assert lib.mq_decode_noalloc(ctypes.byref(params(new, 99, 2)), stream) == 0
+    assert lib.mq_decode_noalloc_fetch(ctypes.byref(tok_err), ctypes.byref(err), ctypes.byref(info), stream) == 0
+    torch.cuda.synchronize()
+    assert err.value == 0
+    assert tok_err.value == int(new["tok"].item()) == int(ref["tok"].item())
+    assert (new["logits"] - ref["logits"]).abs().max().item() <= LOGIT_MAX_ABS
