@@ -388,6 +388,34 @@ def run_batch(args, w, cos, sin, dev, hbm, world):
     return batch
 
 
+def run_tp(args, w, cos, sin, dev, world, prompt):
+    """One sequence decoded by all ranks together (tensor parallel over kv
+    heads, partials exchanged by the kernel over NVLink): tok/s of that one
+    sequence, device-fed tokens, max over ranks of the CUDA-event time."""
+    from megaqwen_b200.tp import make_tp_decoder
+    n = args.steps
+    S = len(prompt) + args.warmup + n + 16
+    dec = make_tp_decoder(w, cos, sin, 28, S)
+    for t in prompt[:-1]:
+        dec.decode_step(t)
+    buf = torch.tensor([prompt[-1]], dtype=torch.int32, device=dev)
+    for _ in range(args.warmup):
+        dec.decode_step_async(buf.data_ptr(), buf.data_ptr())
+    dec.check()
+    barrier(world)
+    tot = time_device_steps(dec, buf, n)
+    dec.check()
+    ms = max_over_ranks(tot, world) / n
+    p_mid = len(prompt) + args.warmup + n // 2
+    per_gpu = bytes_per_token(p_mid) / world
+    hbm, _ = measured_hbm_gbs()
+    del dec
+    return {"tp": world, "tok_s": round(1000.0 / ms, 1), "ms_per_step": round(ms, 5),
+            "roofline_frac_per_gpu": round(per_gpu / (ms / 1000.0) / 1e9 / hbm, 4),
+            "what": "one sequence, kv heads sharded over the ranks, per-layer O/down partials and the argmax "
+                    "exchanged by the decode kernel itself (NVLink peer stores)"}
+
+
 def run_ours(args, rank, world, local):
     import megaqwen_b200
     from megaqwen_b200.weights import make_weights, rope_tables, seeded_prompt
@@ -479,6 +507,11 @@ def run_ours(args, rank, world, local):
     else:
         sweep_prefill = None
 
+    # --- batch-1 KV-head tensor-parallel decode over all ranks (config 5, TP-N) ---
+    tp_leg = None
+    if world in (2, 4, 8) and not args.no_tp:
+        tp_leg = run_tp(args, w, cos, sin, dev, world, prompt)
+
     # --- batched decode (config 5): B independent sequences per GPU, one token each per step ---
     batch = run_batch(args, w, cos, sin, dev, hbm, world) if args.batch_sizes else {}
 
@@ -517,6 +550,7 @@ def run_ours(args, rank, world, local):
             "positions": sweep,
             "prefill": sweep_prefill,
             "batch_decode": batch or None,
+            "tp_decode": tp_leg,
             "reference_megakernel_sm100a": ref_mk,
             "cpu_baseline": cpu,
         }
@@ -540,6 +574,7 @@ def main():
     ap.add_argument("--prefill-batches", type=lambda s: [int(x) for x in s.split(",") if x], default=[1, 8])
     ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel batch-1 leg at N > 1")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-ref-megakernel", action="store_true",
                     help="skip timing the reference megakernel built for sm_100a (oracle/_ref)")

@@ -35,6 +35,7 @@ extern "C" {
 #define MQ_HEAD_DIM 128
 #define MQ_VOCAB_SIZE 151936
 #define MQ_MAX_LAYERS 63
+#define MQ_MAX_TP 8          /* largest tensor-parallel group of mq_decode */
 
 /* Per-layer weight pointers, same field order and size as the reference's
  * LDGLayerWeights (fused_decode_ldg.cu:24-36) and PrefillLayerWeights
@@ -153,6 +154,23 @@ typedef struct mq_decode_params {
                                       written when the step fails before its argmax: wait with a
                                       bound and fall back to mq_decode_fetch.  NULL: off */
     unsigned int host_seq;
+    /* KV-head tensor parallel decode, one rank per GPU (no counterpart in the
+       reference, which runs on one GPU).  tp_size 0 or 1: single GPU.  tp_size
+       T in {2, 4, 8}: rank r = tp_rank computes the q/k/v rows and attention of
+       kv heads [8r/T, 8(r+1)/T), the O and down projections over its own
+       attention / act columns (row-parallel partials), gate/up rows
+       [3072r/T, 3072(r+1)/T) and vocabulary rows [151936r/T, 151936(r+1)/T); it
+       reads only those parts of the full-size weight tensors and writes only
+       its heads' cache rows.  The kernel stores the per-layer O and down
+       partials and the argmax keys into every rank's workspace itself (peer
+       stores over NVLink), and every rank adds the partials in rank order.
+       peer_workspaces: HOST array of T device addresses, valid in this
+       process (CUDA IPC or peer access), of every rank's workspace, entry
+       tp_rank being `workspace`.  The ranks launch the same steps (same token
+       and position) and zero their workspaces together. */
+    int tp_rank;
+    int tp_size;
+    void* const* peer_workspaces;
 } mq_decode_params;
 
 size_t mq_decode_workspace_bytes(void);
@@ -185,7 +203,7 @@ int mq_decode(const mq_decode_params* params, cudaStream_t stream);
  * device index for the life of the process: after cudaDeviceReset() (or any
  * new primary context) this entry point must not be used again.  Calls no
  * cudaMalloc, cudaFree or other allocating routine. */
-#define MQ_NOALLOC_SCRATCH_BYTES 721152
+#define MQ_NOALLOC_SCRATCH_BYTES 950656
 int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream);
 /* Clear the static scratch of the current device (stream-ordered, no
  * allocation), e.g. after a step reported an error.  No-op before the first

@@ -38,6 +38,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -64,22 +65,23 @@ constexpr int NTHREADS = NCT + 32;         // + one producer warp
 constexpr int STAGE_BYTES = 32768;
 constexpr int NSTAGES = 5;
 constexpr int MAX_CTAS = 256;
+constexpr int MAX_TP = MQ_MAX_TP;          // largest tensor-parallel group
 constexpr int CMAX = MAX_CTAS / NKV;       // max position chunks per kv head
 static_assert(CMAX <= 32, "the split-K combine holds one unit per lane");
 constexpr int PART_STRIDE = 132;           // tagged words per (unit, head): acc[128], m, l, pad, pad
 
 constexpr int cmin(int a, int b) { return a < b ? a : b; }
 constexpr int QKV_TILE = cmin(NCW, STAGE_BYTES / (H * 2));      // 15 rows
-constexpr int O_TILE = cmin(NCW, STAGE_BYTES / (QS * 2));       // 8 rows
+constexpr int O_TILE = cmin(NCW, STAGE_BYTES / (QS * 2));       // 8 rows (T = 1; rows per stage are TP_(o_tile, O_TILE))
 constexpr int GU_TILE = cmin(NCW, STAGE_BYTES / (2 * H * 2));   // 8 gate+up row pairs
-constexpr int DOWN_TILE = cmin(NCW, STAGE_BYTES / (I * 2));     // 5 rows
+constexpr int DOWN_TILE = cmin(NCW, STAGE_BYTES / (I * 2));     // 5 rows (T = 1; rows per stage are TP_(dn_tile, DOWN_TILE))
 constexpr int LM_TILE = cmin(NCW, STAGE_BYTES / (H * 2));       // 15 rows
 constexpr int HPT = (H + NCT - 1) / NCT;             // hidden elements per consumer thread (3)
 constexpr int MV_GROUP = 3;                          // ring stages consumed together by a matvec phase
 constexpr int MV_Q = 3;                              // rows per warp in a group
 static_assert(MV_GROUP * QKV_TILE <= MV_Q * NCW && MV_GROUP * LM_TILE <= MV_Q * NCW &&
-              MV_GROUP * GU_TILE <= MV_Q * NCW && MV_GROUP * O_TILE <= MV_Q * NCW &&
-              MV_GROUP * DOWN_TILE <= MV_Q * NCW, "a group's rows fit MV_Q rows per warp");
+              MV_GROUP * GU_TILE <= MV_Q * NCW && MV_GROUP * NCW <= MV_Q * NCW,
+              "a group's rows fit MV_Q rows per warp (O and down stages hold at most NCW rows)");
 static_assert(MV_GROUP < NSTAGES, "the producer can fill a whole group");
 constexpr int KV_TILE = STAGE_BYTES / (2 * D * 2);   // 64 positions (K and V)
 static_assert(KV_TILE == 64 && 4 * MV_GROUP <= NCW, "attention: 4 groups of 16 positions per tile, one warp each");
@@ -113,11 +115,15 @@ static_assert(sizeof(Control) == 256, "control block is 256 bytes");
 constexpr size_t OFF_CTRL = 0;
 constexpr size_t OFF_QKV = 256;
 constexpr size_t OFF_ATTN = OFF_QKV + 2ull * QKV * 8;
+// O-projection and down-projection outputs are per-rank partials
+// [parity][rank][1024] (one rank: the whole vector); every rank stores its
+// partial into every rank's workspace and the consumer adds them in rank order.
 constexpr size_t OFF_HMID = OFF_ATTN + 2ull * QS * 8;
-constexpr size_t OFF_ACT = OFF_HMID + 2ull * H * 8;
+constexpr size_t OFF_ACT = OFF_HMID + 2ull * MAX_TP * H * 8;
 constexpr size_t OFF_HOUT = OFF_ACT + 2ull * I * 8;
-constexpr size_t OFF_PART = OFF_HOUT + 2ull * H * 8;
-constexpr size_t WS_BYTES = OFF_PART + (size_t)NKV * CMAX * 2 * PART_STRIDE * 8;
+constexpr size_t OFF_PART = OFF_HOUT + 2ull * MAX_TP * H * 8;
+constexpr size_t OFF_LMX = OFF_PART + (size_t)NKV * CMAX * 2 * PART_STRIDE * 8;   // [MAX_TP] {key, tag}
+constexpr size_t WS_BYTES = OFF_LMX + (size_t)MAX_TP * 16;
 
 // ---- shared memory layout (bytes, dynamic) -------------------------------------
 constexpr int SM_STAGES = 0;
@@ -136,8 +142,8 @@ constexpr int SM_FLAGS = SM_BEST + 2 * NCW * 4;           // int [4]
 constexpr int SM_BARS = SM_FLAGS + 16;                    // uint64 full[NSTAGES], empty[NSTAGES]
 constexpr int SM_LAYERS = SM_BARS + 2 * NSTAGES * 8;      // LDGLayerWeights [num_layers] copy
 constexpr int SM_SCHED = SM_LAYERS + MQ_MAX_LAYERS * (int)sizeof(LDGLayerWeights);  // Sched
-constexpr int SM_PARAMS = SM_SCHED + 128;                 // KParams copy (see decode_step_kernel)
-constexpr int SMEM_BYTES = SM_PARAMS + 256;
+constexpr int SM_PARAMS = SM_SCHED + 256;                 // KParams copy (see decode_step_kernel)
+constexpr int SMEM_BYTES = SM_PARAMS + 512;
 static_assert(SM_ACC + (NCW + 1) * 2 * D * 4 <= SM_H, "attention combine scratch fits in X+H2");
 static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 static_assert(SM_BARS % 8 == 0, "mbarrier alignment");
@@ -171,8 +177,10 @@ struct KParams {
     unsigned long long* trace;
     mq_host_result* host_result;   // mapped host memory (device-visible address) or null
     uint32_t host_seq;
+    int rank, tp;                  // tensor-parallel rank and group size (1: single GPU)
+    uint8_t* peer_ws[MAX_TP];      // every rank's workspace; [rank] == ws
 };
-static_assert(sizeof(KParams) <= 256 && sizeof(KParams) % 4 == 0, "KParams copy fits its slot");
+static_assert(sizeof(KParams) <= 512 && sizeof(KParams) % 4 == 0, "KParams copy fits its slot");
 
 // Per-CTA slice of every phase (identical on the producer and consumer side).
 struct Sched {
@@ -181,9 +189,19 @@ struct Sched {
     int tag_base;                     // (epoch + 1) << 6
     int qkv_a, qkv_b, o_a, o_b, gu_a, gu_b, dn_a, dn_b, lm_a, lm_b;
     int has_unit, ug, uj, C, kv_s, kv_e, last;
+    // tensor parallel: rank, group size, this rank's q/k rows per matrix
+    // (QS/T, KVS/T), first q/k row, O input columns (QS/T from column q0),
+    // act columns [ia_a, ia_a + ia) of the down projection, rows per O and
+    // down stage
+    int rank, tp, qt, kt, q0, k0, ia_a, ia, o_tile, dn_tile;
 };
 
-static_assert(sizeof(Sched) <= 128, "Sched fits its shared-memory slot");
+static_assert(sizeof(Sched) <= 256, "Sched fits its shared-memory slot");
+
+// Tensor-parallel geometry in code templated on MT (multi-GPU): the
+// single-GPU instantiation (MT == false) sees compile-time constants, so its
+// code is that of a kernel without tensor parallelism.
+#define TP_(field, single) (MT ? S.field : (single))
 
 // Dynamic shared memory of the decode kernel.  Everything a CTA keeps on chip
 // is addressed from this base with the SM_* offsets above, so no pointer to it
@@ -207,14 +225,37 @@ __device__ __forceinline__ uint64_t* ll_qkv(const KParams& P, int l) {
 __device__ __forceinline__ uint64_t* ll_attn(const KParams& P, int l) {
     return reinterpret_cast<uint64_t*>(P.ws + OFF_ATTN) + (size_t)(l & 1) * QS;
 }
+// Partials of rank 0; rank r's follow at + r * H.
+__device__ __forceinline__ size_t off_hmid(int l) { return OFF_HMID + (size_t)(l & 1) * MAX_TP * H * 8; }
+__device__ __forceinline__ size_t off_hout(int l) { return OFF_HOUT + (size_t)(l & 1) * MAX_TP * H * 8; }
 __device__ __forceinline__ uint64_t* ll_hmid(const KParams& P, int l) {
-    return reinterpret_cast<uint64_t*>(P.ws + OFF_HMID) + (size_t)(l & 1) * H;
+    return reinterpret_cast<uint64_t*>(P.ws + off_hmid(l));
 }
 __device__ __forceinline__ uint64_t* ll_act(const KParams& P, int l) {
     return reinterpret_cast<uint64_t*>(P.ws + OFF_ACT) + (size_t)(l & 1) * I;
 }
 __device__ __forceinline__ uint64_t* ll_hout(const KParams& P, int l) {
-    return reinterpret_cast<uint64_t*>(P.ws + OFF_HOUT) + (size_t)(l & 1) * H;
+    return reinterpret_cast<uint64_t*>(P.ws + off_hout(l));
+}
+__device__ __forceinline__ uint64_t* lmx_of(uint8_t* ws, int r) {
+    return reinterpret_cast<uint64_t*>(ws + OFF_LMX) + 2 * r;
+}
+// Tagged words that other GPUs write or read are accessed at system scope.
+__device__ __forceinline__ void st_relaxed_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_relaxed_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys_u64(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
 }
 // Split-K partial of unit j, head h of kv head g as tagged words: acc[128]
 // (unnormalised), max (log2 domain) at 128, sum at 129.
@@ -271,52 +312,71 @@ __device__ __forceinline__ const char* qkv_row(const LDGLayerWeights& W, int r) 
     return (const char*)W.v_proj_weight + (size_t)(r - QS - KVS) * H * 2;
 }
 
+// Row j of this rank's [q; k; v] rows -> its row in the concatenated
+// [q (2048); k (1024); v (1024)] space (one rank: the identity).
+template <bool MT>
+__device__ __forceinline__ int qkv_global(const Sched& S, int j) {
+    if (j < TP_(qt, QS)) return TP_(q0, 0) + j;
+    if (j < TP_(qt, QS) + TP_(kt, KVS)) return QS + TP_(k0, 0) + (j - TP_(qt, QS));
+    return QS + KVS + TP_(k0, 0) + (j - TP_(qt, QS) - TP_(kt, KVS));
+}
+
 // ---- the per-CTA tile lists, shared by producer and consumers ------------------
-// for_tiles calls f(first_row, rows, src1, bytes1, src2, bytes2) for every
-// stage-sized tile this CTA owns in one phase of one layer, in ring order.
-template <class F>
+// for_tiles calls f(first_row, rows, src1, bytes1, src2, bytes2, stride) for
+// every stage-sized tile this CTA owns in one phase of one layer, in ring
+// order.  stride == 0: one or two contiguous copies placed back to back;
+// stride > 0: `rows` rows of bytes1 bytes, stride bytes apart in global
+// memory, packed in the stage.
+template <bool MT, class F>
 __device__ __forceinline__ void for_tiles(const KParams& P, const Sched& S, int phase, int l, F&& f) {
     if (phase == PH_LM) {
         for (int r = S.lm_a; r < S.lm_b;) {
             int n = min(S.lm_b - r, LM_TILE);
-            f(r, n, (const char*)P.lm_head + (size_t)r * H * 2, n * H * 2, (const char*)nullptr, 0);
+            f(r, n, (const char*)P.lm_head + (size_t)r * H * 2, n * H * 2, (const char*)nullptr, 0, 0);
             r += n;
         }
         return;
     }
     const LDGLayerWeights& W = sm<LDGLayerWeights>(SM_LAYERS)[l];
     if (phase == PH_QKV) {
-        // Rows of the concatenated [q; k; v] space in tiles of QKV_TILE; a tile
-        // that crosses a matrix boundary is two bulk copies into one stage.
+        // This rank's rows of [q; k; v] in tiles of QKV_TILE; a tile that
+        // crosses a matrix boundary is two bulk copies into one stage.
+        const int b1 = TP_(qt, QS), b2 = TP_(qt, QS) + TP_(kt, KVS);
         for (int r = S.qkv_a; r < S.qkv_b; r += QKV_TILE) {
             const int e = min(S.qkv_b, r + QKV_TILE);
-            const int cut = (r < QS && e > QS) ? QS : ((r < QS + KVS && e > QS + KVS) ? QS + KVS : e);
-            f(r, e - r, qkv_row(W, r), (cut - r) * H * 2, cut < e ? qkv_row(W, cut) : (const char*)nullptr,
-              (e - cut) * H * 2);
+            const int cut = (r < b1 && e > b1) ? b1 : ((r < b2 && e > b2) ? b2 : e);
+            f(r, e - r, qkv_row(W, qkv_global<MT>(S, r)), (cut - r) * H * 2,
+              cut < e ? qkv_row(W, qkv_global<MT>(S, cut)) : (const char*)nullptr, (e - cut) * H * 2, 0);
         }
     } else if (phase == PH_ATTN) {
         for (int t = S.kv_s; t < S.kv_e; t += KV_TILE) {
             int n = min(S.kv_e - t, KV_TILE);
             size_t off = (((size_t)l * NKV + S.ug) * P.max_seq_len + t) * D * 2;
-            f(t, n, (const char*)P.k_cache + off, n * D * 2, (const char*)P.v_cache + off, n * D * 2);
+            f(t, n, (const char*)P.k_cache + off, n * D * 2, (const char*)P.v_cache + off, n * D * 2, 0);
         }
     } else if (phase == PH_O) {
+        // rows [o_a, o_b) x this rank's attention columns [q0, q0 + qt)
         for (int r = S.o_a; r < S.o_b;) {
-            int n = min(S.o_b - r, O_TILE);
-            f(r, n, (const char*)W.o_proj_weight + (size_t)r * QS * 2, n * QS * 2, (const char*)nullptr, 0);
+            int n = min(S.o_b - r, TP_(o_tile, O_TILE));
+            const char* src = (const char*)W.o_proj_weight + ((size_t)r * QS + TP_(q0, 0)) * 2;
+            if (TP_(tp, 1) == 1) f(r, n, src, n * QS * 2, (const char*)nullptr, 0, 0);
+            else f(r, n, src, TP_(qt, QS) * 2, (const char*)nullptr, 0, QS * 2);
             r += n;
         }
     } else if (phase == PH_GU) {
         for (int r = S.gu_a; r < S.gu_b;) {
             int n = min(S.gu_b - r, GU_TILE);
             f(r, n, (const char*)W.gate_proj_weight + (size_t)r * H * 2, n * H * 2,
-              (const char*)W.up_proj_weight + (size_t)r * H * 2, n * H * 2);
+              (const char*)W.up_proj_weight + (size_t)r * H * 2, n * H * 2, 0);
             r += n;
         }
     } else {
+        // rows [dn_a, dn_b) x this rank's act columns [ia_a, ia_a + ia)
         for (int r = S.dn_a; r < S.dn_b;) {
-            int n = min(S.dn_b - r, DOWN_TILE);
-            f(r, n, (const char*)W.down_proj_weight + (size_t)r * I * 2, n * I * 2, (const char*)nullptr, 0);
+            int n = min(S.dn_b - r, TP_(dn_tile, DOWN_TILE));
+            const char* src = (const char*)W.down_proj_weight + ((size_t)r * I + TP_(ia_a, 0)) * 2;
+            if (TP_(tp, 1) == 1) f(r, n, src, n * I * 2, (const char*)nullptr, 0, 0);
+            else f(r, n, src, TP_(ia, I) * 2, (const char*)nullptr, 0, I * 2);
             r += n;
         }
     }
@@ -336,6 +396,7 @@ __device__ __forceinline__ void walk(const KParams& P, const Sched& S, Vis& v) {
 }
 
 // ---- producer: one thread issuing bulk copies into the stage ring ---------------
+template <bool MT>
 struct Producer {
     const KParams& P;
     uint8_t* smem;
@@ -353,14 +414,17 @@ struct Producer {
         policy = policy_evict_first();
     }
     __device__ __forceinline__ bool run(int phase, int l) {
-        for_tiles(P, *sm<Sched>(SM_SCHED), phase, l,
-                  [&](int, int, const char* s1, int b1, const char* s2, int b2) { tile(phase, l, s1, b1, s2, b2); });
+        for_tiles<MT>(P, *sm<Sched>(SM_SCHED), phase, l,
+                  [&](int, int rows, const char* s1, int b1, const char* s2, int b2, int stride) {
+                      tile(phase, l, s1, b1, s2, b2, stride, rows);
+                  });
         return ok;
     }
 
     // Out of line: one copy of the issue code serves all six tile loops (a
     // smaller producer leaves more of the instruction cache to the consumers).
-    __device__ __noinline__ void tile(int phase, int layer, const char* src1, int b1, const char* src2, int b2) {
+    __device__ __noinline__ void tile(int phase, int layer, const char* src1, int b1, const char* src2, int b2,
+                                      int stride, int rows) {
         if (!ok) return;
         const uint32_t s = n % NSTAGES;
         if (n >= (uint32_t)NSTAGES) {
@@ -382,9 +446,16 @@ struct Producer {
         }
         uint8_t* dst = smem + SM_STAGES + s * STAGE_BYTES;
         if (kGT && P.trace && n < 320) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 512 + 4 * n] = globaltimer_ns();
-        mbar_arrive_expect_tx(&full[s], (uint32_t)(b1 + b2));
-        bulk_g2s(dst, src1, (uint32_t)b1, &full[s], policy);
-        if (b2) bulk_g2s(dst + b1, src2, (uint32_t)b2, &full[s], policy);
+        if (stride) {
+            // strided rows (tensor-parallel column slices): one copy per row
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(rows * b1));
+            for (int i = 0; i < rows; ++i)
+                bulk_g2s(dst + (size_t)i * b1, src1 + (size_t)i * stride, (uint32_t)b1, &full[s], policy);
+        } else {
+            mbar_arrive_expect_tx(&full[s], (uint32_t)(b1 + b2));
+            bulk_g2s(dst, src1, (uint32_t)b1, &full[s], policy);
+            if (b2) bulk_g2s(dst + b1, src2, (uint32_t)b2, &full[s], policy);
+        }
         ++n;
     }
 
@@ -443,6 +514,7 @@ struct LmBest {
 };
 
 // ---- consumers: 16 warps computing on staged tiles -------------------------------
+template <bool MT>
 struct Consumer {
     const KParams& P;
     const Sched& S;
@@ -512,6 +584,75 @@ struct Consumer {
         st_relaxed_u64(p, w);
     }
 
+    // Store one tagged word at byte offset `off` of every rank's workspace
+    // (one rank: its own, gpu scope; several: system scope over NVLink).
+    __device__ __forceinline__ void publish_all(size_t off, uint64_t w) {
+        if (TP_(tp, 1) == 1) {
+            st_relaxed_u64(reinterpret_cast<uint64_t*>(P.ws + off), w);
+            return;
+        }
+        for (int r = 0; r < TP_(tp, 1); ++r) st_relaxed_sys_u64(reinterpret_cast<uint64_t*>(P.peer_ws[r] + off), w);
+    }
+
+    // vals[k] = base[i] + the ranks' partials of element i = ct + k*NCT
+    // (src0: rank 0's tagged words, rank r's at + r*H), added in rank order
+    // so that every CTA of every rank gets bit-identical sums.  Ranks are
+    // polled four at a time, all their words in flight together.
+    template <int NK>
+    __device__ __forceinline__ void poll_sum(const uint64_t* src0, uint32_t tag, const float* base, float* vals,
+                                             uint32_t info) {
+        if (!MT) {
+            float part[NK];
+            poll<NK>(src0, H, tag, part, info);
+#pragma unroll
+            for (int k = 0; k < NK; ++k) vals[k] = (ct + k * NCT < H) ? base[ct + k * NCT] + part[k] : 0.f;
+            return;
+        }
+#pragma unroll
+        for (int k = 0; k < NK; ++k) vals[k] = (ct + k * NCT < H) ? base[ct + k * NCT] : 0.f;
+        const bool sys = TP_(tp, 1) > 1;
+        for (int r0 = 0; r0 < TP_(tp, 1); r0 += 4) {
+            const int nr = min(4, TP_(tp, 1) - r0);
+            float part[NK * 4];
+            uint32_t pending = 0;
+#pragma unroll
+            for (int k = 0; k < NK; ++k)
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    part[k * 4 + q] = 0.f;
+                    if (q < nr && ct + k * NCT < H) pending |= 1u << (k * 4 + q);
+                }
+            uint64_t t0 = 0;
+            uint32_t spins = 0;
+            while (ok && pending) {
+                uint64_t w[NK * 4];
+#pragma unroll
+                for (int j = 0; j < NK * 4; ++j)
+                    if (pending & (1u << j)) {
+                        const uint64_t* a = src0 + (size_t)(r0 + (j & 3)) * H + ct + (j >> 2) * NCT;
+                        w[j] = sys ? ld_relaxed_sys_u64(a) : ld_relaxed_u64(a);
+                    }
+#pragma unroll
+                for (int j = 0; j < NK * 4; ++j)
+                    if ((pending & (1u << j)) && (uint32_t)(w[j] >> 32) == tag) {
+                        part[j] = __uint_as_float((uint32_t)w[j]);
+                        pending &= ~(1u << j);
+                    }
+                if (pending && ((++spins & 31u) == 0)) {
+                    uint64_t now = globaltimer_ns();
+                    if (t0 == 0) t0 = now;
+                    if (flags()[0] != 0 || global_error(P)) { ok = false; break; }
+                    if ((long long)(now - t0) > P.timeout_ns) { fail(MQ_ERR_WAIT_TIMEOUT, info); break; }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < NK; ++k)
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (q < nr) vals[k] += part[k * 4 + q];
+        }
+    }
+
     // Collective: all consumer threads agree on failure.
     __device__ __forceinline__ bool agree() {
         bool bad = named_bar_or(BAR_CONSUMERS, NCT, !ok);
@@ -576,10 +717,12 @@ struct Consumer {
                 for (int k = 0; k < HPT; ++k)
                     if (ct + k * NCT < H) v[k] = __bfloat162float(row[ct + k * NCT]);
             } else {
-                // one call site: the poll loop is inlined once per phase kind
+                // one call site: the poll loop is inlined once per phase kind.
+                // GU: h + the ranks' O partials; QKV / LM: the post-attention
+                // residual + the ranks' down partials of the previous layer.
                 const bool gu = phase == PH_GU;
-                poll<HPT>(gu ? ll_hmid(P, l) : ll_hout(P, l - 1), H, tag_of(S, gu ? l : l - 1), v,
-                          ((uint32_t)phase << 8) | l);
+                poll_sum<HPT>(gu ? ll_hmid(P, l) : ll_hout(P, l - 1), tag_of(S, gu ? l : l - 1), gu ? sh() : sh2(), v,
+                              ((uint32_t)phase << 8) | l);
             }
             micro(l, phase, 1);
             float* res = (phase == PH_GU) ? sh2() : sh();
@@ -612,8 +755,8 @@ struct Consumer {
             return true;
         }
         if (KIND == 3) {
-            const int K = (phase == PH_O) ? QS : I;
-            const uint64_t* src = (phase == PH_O) ? ll_attn(P, l) : ll_act(P, l);
+            const int K = (phase == PH_O) ? TP_(qt, QS) : TP_(ia, I);     // this rank's attention / act slice
+            const uint64_t* src = (phase == PH_O) ? ll_attn(P, l) + TP_(q0, 0) : ll_act(P, l) + TP_(ia_a, 0);
             named_bar_sync(BAR_CONSUMERS, NCT);   // the previous phase is done with X
             int cnt = poll<(I + NCT - 1) / NCT>(src, K, tag_of(S, l), v, ((uint32_t)phase << 8) | l);
             micro(l, phase, 1);
@@ -833,14 +976,14 @@ struct Consumer {
     template <int KIND, int phase>
     __device__ __forceinline__ void mv_phase(int l, const float* xr, LmBest* bst) {
         int a, b;
-        constexpr int T = phase == PH_QKV ? QKV_TILE : phase == PH_GU ? GU_TILE : phase == PH_O ? O_TILE
-                          : phase == PH_DOWN ? DOWN_TILE : LM_TILE;
+        const int T = phase == PH_QKV ? QKV_TILE : phase == PH_GU ? GU_TILE : phase == PH_O ? TP_(o_tile, O_TILE)
+                      : phase == PH_DOWN ? TP_(dn_tile, DOWN_TILE) : LM_TILE;
         if (phase == PH_QKV) { a = S.qkv_a; b = S.qkv_b; }
         else if (phase == PH_GU) { a = S.gu_a; b = S.gu_b; }
         else if (phase == PH_O) { a = S.o_a; b = S.o_b; }
         else if (phase == PH_DOWN) { a = S.dn_a; b = S.dn_b; }
         else { a = S.lm_a; b = S.lm_b; }
-        constexpr int K = (phase == PH_O) ? QS : (phase == PH_DOWN ? I : H);
+        const int K = (phase == PH_O) ? TP_(qt, QS) : (phase == PH_DOWN ? TP_(ia, I) : H);
         const int R = b - a;
         const int ntiles = (R + T - 1) / T;
         const uint32_t tag = tag_of(S, l);
@@ -879,14 +1022,12 @@ struct Consumer {
                                 if (KIND == 0 && phase == PH_GU) dot8x2(u2, wu[c], lo, hi);
                             }
                         } else {
-                            const uint4* w = reinterpret_cast<const uint4*>(st + lr * K * 2);
-                            constexpr int CPL = K / 256;
+                            const uint4* w = reinterpret_cast<const uint4*>(st + (size_t)lr * K * 2);
+                            const int chunks = K >> 3;
 #pragma unroll 2
-                            for (int u = 0; u < CPL; ++u) {
-                                const int c = lane + 32 * u;
+                            for (int c = lane; c < chunks; c += 32)
                                 dot8x2(a2, w[c], *reinterpret_cast<const float4*>(sx() + c * 4),
                                        *reinterpret_cast<const float4*>(sx() + K / 2 + c * 4));
-                            }
                         }
                         acc[q] = f2sum(a2);
                         if (KIND == 0 && phase == PH_GU) up[q] = f2sum(u2);
@@ -915,11 +1056,12 @@ struct Consumer {
                         } else if (phase == PH_GU) {
                             ll_store(ll_act(P, l) + r, ll_word(v / (1.0f + expf(-v)) * (up[q] * nrm), tag));
                         } else if (phase == PH_QKV) {
-                            if (!((S.c == P.inject_skip_cta - 1) && l == 0)) ll_store(ll_qkv(P, l) + r, ll_word(v, tag));
+                            if (!((S.c == P.inject_skip_cta - 1) && l == 0))
+                                ll_store(ll_qkv(P, l) + qkv_global<MT>(S, r), ll_word(v, tag));
                         } else if (phase == PH_O) {
-                            ll_store(ll_hmid(P, l) + r, ll_word(v + sh()[r], tag));
+                            publish_all(off_hmid(l) + ((size_t)TP_(rank, 0) * H + r) * 8, ll_word(v, tag));
                         } else {
-                            ll_store(ll_hout(P, l) + r, ll_word(v + sh2()[r], tag));
+                            publish_all(off_hout(l) + ((size_t)TP_(rank, 0) * H + r) * 8, ll_word(v, tag));
                         }
                     }
                 }
@@ -1240,8 +1382,32 @@ struct Consumer {
             if (old == (uint32_t)(S.G - 1)) {
                 __threadfence();
                 unsigned long long best = atomicExch(&C->lm_best, 0ull);
-                int tok = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
                 atomicExch(&C->lm_count, 0u);
+                if (TP_(tp, 1) > 1) {
+                    // the ranks' best keys: {key, tag} into every rank's slot,
+                    // then the maximum over all slots (bounded waits)
+                    const uint64_t stag = (uint64_t)(uint32_t)S.tag_base;
+                    for (int r = 0; r < TP_(tp, 1); ++r) {
+                        uint64_t* slot = lmx_of(P.peer_ws[r], TP_(rank, 0));
+                        st_relaxed_sys_u64(slot, best);
+                        st_release_sys_u64(slot + 1, stag);
+                    }
+                    const uint64_t t0 = globaltimer_ns();
+                    for (int r = 0; r < TP_(tp, 1); ++r) {
+                        const uint64_t* slot = lmx_of(P.ws, r);
+                        uint32_t spins = 0;
+                        while (ld_acquire_sys_u64(slot + 1) != stag) {
+                            if ((++spins & 31u) == 0 &&
+                                (global_error(P) || (long long)(globaltimer_ns() - t0) > P.timeout_ns)) {
+                                if (!global_error(P)) record_error(P, MQ_ERR_WAIT_TIMEOUT, ((uint32_t)PH_LM << 8) | 0x80u);
+                                return;
+                            }
+                        }
+                        const unsigned long long k2 = ld_relaxed_sys_u64(slot);
+                        if (k2 > best) best = k2;
+                    }
+                }
+                int tok = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffull));
                 if (P.output_token) *P.output_token = tok;
                 if (P.host_result) {
                     // token, error, info first, then the sequence word the host waits on
@@ -1265,9 +1431,9 @@ struct Consumer {
 
 // Consumer progress between phase calls: tiles consumed (bits 0-23), block-sum
 // parity (bit 24), this thread failed (bit 25), stop the walk (bit 26).
-template <int KIND>
+template <int KIND, bool MT>
 __device__ __noinline__ uint32_t consumer_phase(const KParams* P, int phase, int l, uint32_t st) {
-    Consumer c(*P, *sm<Sched>(SM_SCHED));
+    Consumer<MT> c(*P, *sm<Sched>(SM_SCHED));
     c.n = st & 0xffffffu;
     c.red_par = (st >> 24) & 1u;
     c.ok = ((st >> 25) & 1u) == 0;
@@ -1277,18 +1443,22 @@ __device__ __noinline__ uint32_t consumer_phase(const KParams* P, int phase, int
 
 // Walk visitor for the consumer warps: each phase kind is its own function so
 // the register allocator sees one phase at a time (no spills).
+template <bool MT>
 struct ConsumerWalk {
     const KParams* P;
     uint32_t st = 0;
     __device__ bool run(int phase, int l) {
-        if (phase == PH_ATTN) st = consumer_phase<1>(P, phase, l, st);
-        else if (phase == PH_LM) st = consumer_phase<2>(P, phase, l, st);
-        else if (phase == PH_O || phase == PH_DOWN) st = consumer_phase<3>(P, phase, l, st);
-        else st = consumer_phase<0>(P, phase, l, st);
+        if (phase == PH_ATTN) st = consumer_phase<1, MT>(P, phase, l, st);
+        else if (phase == PH_LM) st = consumer_phase<2, MT>(P, phase, l, st);
+        else if (phase == PH_O || phase == PH_DOWN) st = consumer_phase<3, MT>(P, phase, l, st);
+        else st = consumer_phase<0, MT>(P, phase, l, st);
         return (st & (1u << 26)) == 0;
     }
 };
 
+// MT: the tensor-parallel instantiation (tp_size > 1); the single-GPU one is
+// compiled with the partition sizes as constants.
+template <bool MT>
 __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_constant__ KParams P) {
     Control* C = ctrl_of(P);
     volatile int* flags = sm<volatile int>(SM_FLAGS);
@@ -1311,21 +1481,38 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_c
         S.pos = pos;
         S.L = pos + 1;
         S.tag_base = (int)((C->epoch + 1u) << 6);
-        S.qkv_a = split_at(QKV, S.G, S.c); S.qkv_b = split_at(QKV, S.G, S.c + 1);
+        // tensor parallel (T ranks, this one `rank`): q/k/v rows and the
+        // attention of kv heads [8 rank / T, 8 (rank + 1) / T); O and down
+        // rows over this rank's input slice (row-parallel partials); gate/up
+        // rows and LM rows of this rank's slice.  T = 1: the whole model.
+        const int T = P.tp, rk = P.rank;
+        S.tp = T;
+        S.rank = rk;
+        S.qt = QS / T;  S.kt = KVS / T;
+        S.q0 = S.qt * rk; S.k0 = S.kt * rk;
+        S.ia = I / T;   S.ia_a = S.ia * rk;
+        S.o_tile = min(NCW, STAGE_BYTES / (S.qt * 2));
+        S.dn_tile = min(NCW, STAGE_BYTES / (S.ia * 2));
+        const int nq = S.qt + 2 * S.kt;
+        S.qkv_a = split_at(nq, S.G, S.c);  S.qkv_b = split_at(nq, S.G, S.c + 1);
         S.o_a = split_at(H, S.G, S.c);     S.o_b = split_at(H, S.G, S.c + 1);
-        S.gu_a = split_at(I, S.G, S.c);    S.gu_b = split_at(I, S.G, S.c + 1);
+        S.gu_a = S.ia_a + split_at(S.ia, S.G, S.c);
+        S.gu_b = S.ia_a + split_at(S.ia, S.G, S.c + 1);
         S.dn_a = S.o_a;                    S.dn_b = S.o_b;
-        S.lm_a = split_at(V, S.G, S.c);    S.lm_b = split_at(V, S.G, S.c + 1);
+        const int va = (int)((long long)V * rk / T), vb = (int)((long long)V * (rk + 1) / T);
+        S.lm_a = va + split_at(vb - va, S.G, S.c);
+        S.lm_b = va + split_at(vb - va, S.G, S.c + 1);
         const int chunk = P.attn_chunk > 0 ? P.attn_chunk : 64;
         int C_ = (S.L + chunk - 1) / chunk;
-        C_ = min(C_, S.G / NKV);
+        const int NH = NKV / T;   // kv heads of this rank
+        C_ = min(C_, S.G / NH);
         C_ = min(C_, CMAX);
         C_ = max(C_, 1);
         S.C = C_;
-        const int U = NKV * C_;
+        const int U = NH * C_;
         const int u = (int)(((long long)S.c * U + S.G - 1) / S.G);
         S.has_unit = (u < U) && (int)(((long long)u * S.G) / U) == S.c;
-        S.ug = u / C_;
+        S.ug = NH * rk + u / C_;
         S.uj = u % C_;
         const int ps = split_at(S.L, C_, S.uj), pe = split_at(S.L, C_, S.uj + 1);
         S.last = (S.uj == C_ - 1);
@@ -1364,18 +1551,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) decode_step_kernel(const __grid_c
 
     if (threadIdx.x < 32) {
         if (threadIdx.x == 0) {
-            Producer pr(Ps, g_smem);
+            Producer<MT> pr(Ps, g_smem);
             walk(Ps, S, pr);
             if (P.trace) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 502] = globaltimer_ns();
             pr.drain();
         }
         return;
     }
-    ConsumerWalk cs{&Ps};
+    ConsumerWalk<MT> cs{&Ps};
     if (P.trace && threadIdx.x == 32) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 500] = globaltimer_ns();
     walk(Ps, S, cs);
     if (P.trace && threadIdx.x == 32) P.trace[(size_t)blockIdx.x * TRACE_STRIDE + 501] = globaltimer_ns();
 }
+
+#undef TP_
 
 }  // namespace mq
 
@@ -1414,9 +1603,10 @@ bool kernel_configured[64] = {false};
 
 int configure_kernel(int dev) {
     if (dev >= 0 && dev < 64 && kernel_configured[dev]) return MQ_OK;
-    cudaError_t e = cudaFuncSetAttribute(mq::decode_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         mq::SMEM_BYTES);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+    for (auto kern : {mq::decode_step_kernel<false>, mq::decode_step_kernel<true>}) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, mq::SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic shared memory)");
+    }
     if (dev >= 0 && dev < 64) kernel_configured[dev] = true;
     return MQ_OK;
 }
@@ -1459,14 +1649,27 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
         int rc = configure_kernel(dev);
         if (rc) return rc;
         int maxb = 0;
-        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel, mq::NTHREADS, mq::SMEM_BYTES);
+        ce = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&maxb, mq::decode_step_kernel<true>, mq::NTHREADS, mq::SMEM_BYTES);
         if (ce != cudaSuccess) return cuda_fail(ce, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
         if (maxb < 1) return note(MQ_ERR_CUDA, "decode kernel does not fit on one SM (occupancy 0)");
         dev_ctas[dev] = default_ctas(dev);
     }
     int G = p->num_ctas > 0 ? p->num_ctas : dev_ctas[dev];
     if (G < mq::NKV || G > mq::MAX_CTAS) return MQ_ERR_INVALID_ARGUMENT;
+    const int T = p->tp_size > 0 ? p->tp_size : 1;
+    if (T != 1 && T != 2 && T != 4 && T != 8) return note(MQ_ERR_INVALID_ARGUMENT, "tp_size must be 1, 2, 4 or 8");
+    if (p->tp_rank < 0 || p->tp_rank >= T) return note(MQ_ERR_INVALID_ARGUMENT, "tp_rank out of range");
+    if (T > 1 && !p->peer_workspaces) return note(MQ_ERR_INVALID_ARGUMENT, "tp_size > 1 needs peer_workspaces");
     mq::KParams k;
+    std::memset(&k, 0, sizeof(k));
+    k.tp = T;
+    k.rank = p->tp_rank;
+    for (int r = 0; r < T; ++r) {
+        k.peer_ws[r] = T == 1 ? (uint8_t*)p->workspace : (uint8_t*)p->peer_workspaces[r];
+        if (!k.peer_ws[r]) return note(MQ_ERR_INVALID_ARGUMENT, "peer_workspaces holds a null pointer");
+    }
+    if (k.peer_ws[p->tp_rank] != (uint8_t*)p->workspace)
+        return note(MQ_ERR_INVALID_ARGUMENT, "peer_workspaces[tp_rank] must be this rank's workspace");
     k.input_token = p->input_token;
     k.input_token_ptr = p->input_token_ptr;
     k.output_token = p->output_token;
@@ -1504,7 +1707,8 @@ int launch(const mq_decode_params* p, cudaStream_t stream) {
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;   // always cooperative: the CTAs wait on each other, so all must be resident
-    cudaError_t e = cudaLaunchKernelEx(&cfg, mq::decode_step_kernel, k);
+    cudaError_t e = T > 1 ? cudaLaunchKernelEx(&cfg, mq::decode_step_kernel<true>, k)
+                          : cudaLaunchKernelEx(&cfg, mq::decode_step_kernel<false>, k);
     if (e != cudaSuccess) return cuda_fail(e, "cudaLaunchKernelEx(decode_step_kernel, cooperative)");
     return MQ_OK;
 }
@@ -1605,6 +1809,8 @@ int mq_decode_noalloc(const mq_decode_params* params, cudaStream_t stream) {
         return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: num_ctas exceeds the 256 CTAs the static scratch holds");
     if (params->num_layers > MQ_MAX_LAYERS)
         return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: num_layers exceeds the 63 layers the static scratch holds");
+    if (params->tp_size > 1)
+        return note(MQ_ERR_INVALID_ARGUMENT, "mq_decode_noalloc: tensor-parallel steps need caller workspaces (mq_decode)");
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");

@@ -251,6 +251,13 @@ protected:
         p.timeout_ns = timeout_ns_;
         p.inject_skip_cta = inject_skip_cta_;
         p.trace = trace_;
+        if (tp_size_ > 1) {
+            for (void* q : peer_ws_)
+                if (!q) throw std::runtime_error("tensor-parallel decoder is not connected to every rank (connect)");
+            p.tp_rank = tp_rank_;
+            p.tp_size = tp_size_;
+            p.peer_workspaces = peer_ws_.data();
+        }
         return p;
     }
 
@@ -347,6 +354,8 @@ protected:
     long long timeout_ns_ = 0;
     int inject_skip_cta_ = 0;
     unsigned long long* trace_ = nullptr;
+    int tp_rank_ = 0, tp_size_ = 1;         // tensor parallel (MegakernelTPDecoder)
+    std::vector<void*> peer_ws_;            // every rank's workspace, device addresses valid here
     mq_host_result* hres_ = nullptr;       // host address of the mapped result
     mq_host_result* hres_dev_ = nullptr;   // its device-visible address
     bool hres_failed_ = false;
@@ -362,6 +371,91 @@ protected:
 // prefill (mq_prefill: tcgen05 GEMMs, flash attention) and writes the K/V
 // cache rows 0..S-1, like the reference's cuBLAS prefill (fused_prefill.cu:
 // 601-867); decode_step then continues at position S.
+// ---------------------------------------------------------------------------
+// KV-head tensor-parallel batch-1 decoder: one instance per rank (one GPU per
+// process), all ranks stepping together.  Same weights and call surface as
+// MegakernelDecoder; the kernel computes this rank's heads, row-parallel
+// partials and vocabulary slice and exchanges partials with the other ranks
+// over NVLink by itself.  The workspace is a plain cudaMalloc allocation so
+// that its CUDA IPC handle (ipc_handle) can be opened by the other ranks
+// (connect).  No counterpart in the reference, which runs on one GPU.
+class MegakernelTPDecoder : public MegakernelDecoder {
+public:
+    MegakernelTPDecoder(torch::Tensor embed_weight, std::vector<torch::Tensor> layer_weights_flat,
+                        torch::Tensor final_norm_weight, torch::Tensor lm_head_weight, torch::Tensor cos_table,
+                        torch::Tensor sin_table, int num_layers, int max_seq_len, int tp_rank, int tp_size)
+        : MegakernelDecoder(embed_weight, layer_weights_flat, final_norm_weight, lm_head_weight, cos_table, sin_table,
+                            num_layers, max_seq_len) {
+        if (tp_size != 1 && tp_size != 2 && tp_size != 4 && tp_size != 8)
+            throw std::runtime_error("tp_size must be 1, 2, 4 or 8");
+        if (tp_rank < 0 || tp_rank >= tp_size) throw std::runtime_error("tp_rank out of range");
+        c10::cuda::CUDAGuard guard(device_);
+        const size_t bytes = mq_decode_workspace_bytes();
+        void* ws = nullptr;
+        if (cudaMalloc(&ws, bytes) != cudaSuccess) throw std::runtime_error("cudaMalloc(tensor-parallel workspace) failed");
+        if (cudaMemset(ws, 0, bytes) != cudaSuccess) throw std::runtime_error("cudaMemset(workspace) failed");
+        own_ws_ = ws;
+        workspace_ = torch::from_blob(ws, {(int64_t)bytes}, torch::dtype(torch::kUInt8).device(device_));
+        tp_rank_ = tp_rank;
+        tp_size_ = tp_size;
+        peer_ws_.assign(tp_size, nullptr);
+        peer_ws_[tp_rank] = ws;
+        opened_.assign(tp_size, false);
+    }
+    ~MegakernelTPDecoder() override {
+        for (int r = 0; r < tp_size_; ++r)
+            if (opened_[r] && peer_ws_[r]) cudaIpcCloseMemHandle(peer_ws_[r]);
+        workspace_ = torch::Tensor();
+        if (own_ws_) cudaFree(own_ws_);
+    }
+
+    // CUDA IPC handle of this rank's workspace (64 bytes), for the other ranks.
+    py::bytes ipc_handle() {
+        c10::cuda::CUDAGuard guard(device_);
+        cudaIpcMemHandle_t h;
+        if (cudaIpcGetMemHandle(&h, own_ws_) != cudaSuccess) throw std::runtime_error("cudaIpcGetMemHandle failed");
+        return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+    }
+
+    // Open every other rank's workspace from its IPC handle (handles[r] for
+    // rank r; this rank's own entry is ignored).
+    void connect(std::vector<std::string> handles) {
+        if ((int)handles.size() != tp_size_) throw std::runtime_error("connect needs one handle per rank");
+        c10::cuda::CUDAGuard guard(device_);
+        for (int r = 0; r < tp_size_; ++r) {
+            if (r == tp_rank_ || opened_[r]) continue;
+            if (handles[r].size() != sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("bad IPC handle size");
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, handles[r].data(), sizeof(h));
+            void* p = nullptr;
+            const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+            if (e != cudaSuccess)
+                throw std::runtime_error(std::string("cudaIpcOpenMemHandle failed: ") + cudaGetErrorString(e));
+            peer_ws_[r] = p;
+            opened_[r] = true;
+        }
+        connected_ = true;
+    }
+
+    // Zero this rank's workspace (all ranks together, between steps, e.g.
+    // after a step failed on any rank).
+    void zero_workspace() {
+        c10::cuda::CUDAGuard guard(device_);
+        mq_decode_workspace_init(own_ws_, mq_decode_workspace_bytes(),
+                                 c10::cuda::getCurrentCUDAStream(device_.index()).stream());
+        cudaStreamSynchronize(c10::cuda::getCurrentCUDAStream(device_.index()).stream());
+    }
+
+    int tp_rank() const { return tp_rank_; }
+    int tp_size() const { return tp_size_; }
+    bool connected() const { return connected_ || tp_size_ == 1; }
+
+private:
+    void* own_ws_ = nullptr;
+    std::vector<bool> opened_;
+    bool connected_ = false;
+};
+
 class MegakernelPrefillDecoder : public MegakernelDecoder {
 public:
     MegakernelPrefillDecoder(torch::Tensor embed_weight, std::vector<torch::Tensor> layer_weights_flat,
@@ -862,6 +956,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("set_timeout_ns", &MegakernelDecoder::set_timeout_ns)
         .def("set_inject_skip_cta", &MegakernelDecoder::set_inject_skip_cta)
         .def("set_trace", &MegakernelDecoder::set_trace);
+    py::class_<MegakernelTPDecoder, MegakernelDecoder>(m, "MegakernelTPDecoder")
+        .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
+                      torch::Tensor, int, int, int, int>(),
+             py::arg("embed_weight"), py::arg("layer_weights"), py::arg("final_norm_weight"),
+             py::arg("lm_head_weight"), py::arg("cos_table"), py::arg("sin_table"), py::arg("num_layers"),
+             py::arg("max_seq_len"), py::arg("tp_rank"), py::arg("tp_size"))
+        .def("ipc_handle", &MegakernelTPDecoder::ipc_handle)
+        .def("connect", &MegakernelTPDecoder::connect)
+        .def("zero_workspace", &MegakernelTPDecoder::zero_workspace)
+        .def("tp_rank", &MegakernelTPDecoder::tp_rank)
+        .def("tp_size", &MegakernelTPDecoder::tp_size)
+        .def("connected", &MegakernelTPDecoder::connected);
     py::class_<MegakernelPrefillDecoder, MegakernelDecoder>(m, "MegakernelPrefillDecoder")
         .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
                       torch::Tensor, int, int, int>(),

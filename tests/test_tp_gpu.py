@@ -1,0 +1,147 @@
+"""KV-head tensor-parallel decode on 2 GPUs (MegakernelTPDecoder, one process
+per GPU, the kernel exchanging partials over NVLink) against the CPU oracle,
+and failure detection across ranks without a GPU fault.  Skipped on hosts
+with fewer than two GPUs.
+
+Bar as for the single-GPU decode: per-step logits max-abs <= 3e-2 and cosine
+>= 0.9995 against the oracle, greedy tokens identical.  Each rank writes the
+logits of its own vocabulary slice; rank 0 joins the slices."""
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_MAX_ABS = 3e-2
+COSINE_MIN = 0.9995
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, num_layers, steps, out):
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from megaqwen_b200.tp import make_tp_decoder, tp_partition
+        from megaqwen_b200.weights import make_weights, rope_tables, seeded_prompt
+        S = 64
+        wc = make_weights(num_layers)
+        wd = wc.to("cuda")
+        cos, sin = rope_tables(S, device="cuda")
+        dec = make_tp_decoder(wd, cos, sin, num_layers, S)
+        v0, v1 = tp_partition(rank, world).vocab_rows
+        o = None
+        if rank == 0:
+            from oracle.qwen3_cpu import Qwen3CpuOracle
+            o = Qwen3CpuOracle(wc, max_seq_len=S)
+        prompt = seeded_prompt(8).tolist()
+        worst, tokens, ref_tokens = 0.0, [], []
+        cur = prompt[0]
+        for i in range(len(prompt) + steps):
+            tok, lg = dec.decode_step_with_logits(cur)
+            parts = [None] * world
+            dist.all_gather_object(parts, (v0, v1, lg[v0:v1].cpu()))
+            if rank == 0:
+                full = torch.empty(151936)
+                for a, b, t in parts:
+                    full[a:b] = t
+                ref = o.decode_step(cur, i)
+                err = (full - ref).abs().max().item()
+                cosv = torch.nn.functional.cosine_similarity(full.view(1, -1), ref.view(1, -1)).item()
+                assert err <= LOGIT_MAX_ABS, f"step {i}: logits max-abs {err}"
+                assert cosv >= COSINE_MIN, f"step {i}: cosine {cosv}"
+                worst = max(worst, err)
+                ref_tokens.append(int(torch.argmax(ref)))
+            tokens.append(tok)
+            cur = prompt[i + 1] if i + 1 < len(prompt) else tok
+        all_tokens = [None] * world
+        dist.all_gather_object(all_tokens, tokens)
+        assert all(t == tokens for t in all_tokens), "ranks disagree on the tokens"
+        if rank == 0:
+            assert tokens == ref_tokens
+        out[rank] = ("ok", worst)
+    except Exception as exc:  # reported to the parent
+        out[rank] = ("fail", repr(exc))
+    finally:
+        dist.destroy_process_group()
+
+
+def _rank_timeout(rank, world, port, out):
+    """Rank 1 withholds its layer-0 q/k/v stores in one step: both ranks' bounded
+    waits run out (rank 0 waits for rank 1's partials), both report the
+    timeout, then all ranks zero their workspaces between steps and the next
+    step is correct again."""
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from megaqwen_b200.tp import make_tp_decoder
+        from megaqwen_b200.weights import make_weights, rope_tables
+        wd = make_weights(2).to("cuda")
+        cos, sin = rope_tables(32, device="cuda")
+        dec = make_tp_decoder(wd, cos, sin, 2, 32)
+        good = dec.decode_step(5)
+        dec.reset()
+        dec.set_timeout_ns(100_000_000)
+        if rank == 1:
+            dec.set_inject_skip_cta(1 + 3)
+        raised = ""
+        try:
+            dec.decode_step(5)
+        except RuntimeError as exc:
+            raised = str(exc)
+        dec.set_inject_skip_cta(0)
+        dist.barrier()                 # every rank's failed step has ended
+        dec.zero_workspace()
+        dec.reset()
+        dist.barrier()
+        again = dec.decode_step(5)
+        out[rank] = ("ok", raised, good, again)
+    except Exception as exc:
+        out[rank] = ("fail", repr(exc), 0, 0)
+    finally:
+        dist.destroy_process_group()
+
+
+def _need_two():
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    if torch.cuda.device_count() < 2:
+        pytest.skip("tensor-parallel decode needs 2 GPUs")
+
+
+@pytest.mark.parametrize("num_layers,steps", [(2, 24), (28, 24)])
+def test_tp2_decode_matches_oracle(num_layers, steps):
+    _need_two()
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    mp.start_processes(_rank, args=(2, _free_port(), num_layers, steps, out), nprocs=2, join=True,
+                       start_method="spawn")
+    for r in range(2):
+        assert out[r][0] == "ok", out[r][1]
+    print(f"TP-2 L={num_layers}: worst logits max-abs {out[0][1]:.3e}")
+
+
+def test_tp2_wait_timeout_is_reported_on_every_rank_and_recoverable():
+    _need_two()
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    mp.start_processes(_rank_timeout, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
+    for r in range(2):
+        status, raised, good, again = out[r]
+        assert status == "ok", raised
+        assert "timed out" in raised, f"rank {r}: {raised!r}"
+        assert again == good

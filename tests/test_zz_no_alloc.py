@@ -37,7 +37,8 @@ class DecodeParams(ctypes.Structure):
         ("position_ptr", ctypes.c_void_p), ("max_seq_len", ctypes.c_int), ("attn_scale", ctypes.c_float),
         ("num_ctas", ctypes.c_int), ("attn_chunk", ctypes.c_int), ("timeout_ns", ctypes.c_longlong),
         ("inject_skip_cta", ctypes.c_int), ("trace", ctypes.c_void_p), ("host_result", ctypes.c_void_p),
-        ("host_seq", ctypes.c_uint),
+        ("host_seq", ctypes.c_uint), ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int),
+        ("peer_workspaces", ctypes.c_void_p),
     ]
 
 
