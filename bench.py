@@ -32,12 +32,13 @@ WEIGHT_BYTES = 1_192_101_888            # 28 layers + lm_head + norms + one embe
 KV_BYTES_PER_POS = 114_688              # K+V, all layers, one position (bf16)
 
 
-# DRAM bytes (read + write) of one decode_step_kernel launch at position ~20 from
-# one `ncu --set full` capture (profiles/decode_step_kernel_config2.md).  DRAM
-# traffic tracks the algorithmic bytes (the same holds at p = 8192,
-# profiles/decode_step_kernel_p8192.md), so the bench scales it to its own mean
-# position by the algorithmic-bytes ratio.
-NCU_TRAFFIC_P20 = 1_194_463_000 + 3_732_736
+# DRAM bytes (read + write) per decode_step_kernel launch at position 19: the
+# mean of three launches captured with ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum, one pass, --clock-control none) on 2026-12-02 from the
+# tree of the tensor-parallel decode commit; traffic / algorithmic bytes =
+# 1.0023.  DRAM traffic tracks the algorithmic bytes, so the bench scales it to
+# its own mean position by the algorithmic-bytes ratio.
+NCU_TRAFFIC_P19 = 1_197_266_432
 
 
 def bytes_per_token(pos: int) -> int:
@@ -540,8 +541,8 @@ def run_ours(args, rank, world, local):
             "gpu_launches": args.steps,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4),
-                         "traffic": round(NCU_TRAFFIC_P20 * bytes_per_token(p_mid) / bytes_per_token(20)),
-                         "traffic_source": "ncu capture at p~20, scaled by algorithmic bytes",
+                         "traffic": round(NCU_TRAFFIC_P19 * bytes_per_token(p_mid) / bytes_per_token(19)),
+                         "traffic_source": "ncu dram__bytes_read+write of the current kernel at p=19 (2026-12-02), scaled by algorithmic bytes",
                          "peak_kind": hbm_kind, "bytes_per_launch": bytes_per_token(p_mid),
                          "launch_ms": round(launch_ms, 5)},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 16,
