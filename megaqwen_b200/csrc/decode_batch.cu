@@ -57,7 +57,7 @@ __device__ __forceinline__ int vdim(int u, int r, int g) { return 32 * u + 8 * (
 // exponentiated scores.  Online softmax in the log2 domain (q pre-scaled by
 // scale * log2 e); the four warps merge through shared memory and the unit
 // writes its (max, sum, unnormalised acc) per q head.
-__global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict__ Qf, const bf16* __restrict__ kc,
+__global__ void __launch_bounds__(128, 4) attn_unit_kernel(const float* __restrict__ Qf, const bf16* __restrict__ kc,
                                                         const bf16* __restrict__ vc, const int* __restrict__ pos,
                                                         long long seq_stride, int max_seq, int C, float scale_log2,
                                                         int chunk, float* __restrict__ part,
@@ -122,11 +122,11 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
             }
         }
     };
-    if (warp < ngroups) load(warp, kr, vr);
+    // Each warp loads one 16-position group at a time straight into registers;
+    // the latency is covered by the other resident warps (4+ CTAs per SM at
+    // <= 128 registers) rather than by a second register buffer.
     for (int grp = warp; grp < ngroups; grp += 4) {
-        uint4 kn[2][4], vn[2][4];
-        const bool more = grp + 4 < ngroups;
-        if (more) load(grp + 4, kn, vn);
+        load(grp, kr, vr);
         // S^T[16 positions][8 heads]
         float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -175,15 +175,6 @@ __global__ void __launch_bounds__(128) attn_unit_kernel(const float* __restrict_
                 const uint32_t a[4] = {movm_t(r0[qq]), movm_t(r0[qq + 2]), movm_t(r1[qq]), movm_t(r1[qq + 2])};
                 pf::mma_bf16(o, a, pb0, pb1);
             }
-        }
-        if (more) {
-#pragma unroll
-            for (int hr = 0; hr < 2; ++hr)
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    kr[hr][u] = kn[hr][u];
-                    vr[hr][u] = vn[hr][u];
-                }
         }
     }
 #pragma unroll
