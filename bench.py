@@ -411,10 +411,30 @@ def run_tp(args, w, cos, sin, dev, world, prompt):
     per_gpu = bytes_per_token(p_mid) / world
     hbm, _ = measured_hbm_gbs()
     del dec
-    return {"tp": world, "tok_s": round(1000.0 / ms, 1), "ms_per_step": round(ms, 5),
-            "roofline_frac_per_gpu": round(per_gpu / (ms / 1000.0) / 1e9 / hbm, 4),
-            "what": "one sequence, kv heads sharded over the ranks, per-layer O/down partials and the argmax "
-                    "exchanged by the decode kernel itself (NVLink peer stores)"}
+    out = {"tp": world, "tok_s": round(1000.0 / ms, 1), "ms_per_step": round(ms, 5),
+           "roofline_frac_per_gpu": round(per_gpu / (ms / 1000.0) / 1e9 / hbm, 4),
+           "what": "one sequence, kv heads sharded over the ranks, per-layer O/down partials and the argmax "
+                   "exchanged by the decode kernel itself (NVLink peer stores)"}
+    # long context (config 3): caches pre-filled with N(0,1) K/V, where one GPU is bandwidth-bound
+    for P in args.tp_long:
+        n2 = args.sweep_steps
+        dec = make_tp_decoder(w, cos, sin, 28, P + n2 + 8)
+        g = torch.Generator(device=dev).manual_seed(11)
+        dec.get_k_cache()[:, :, :P].normal_(generator=g)
+        dec.get_v_cache()[:, :, :P].normal_(generator=g)
+        dec.set_position(P)
+        b2 = torch.tensor([5], dtype=torch.int32, device=dev)
+        for _ in range(3):
+            dec.decode_step_async(b2.data_ptr(), b2.data_ptr())
+        dec.check()
+        barrier(world)
+        t2 = time_device_steps(dec, b2, n2)
+        dec.check()
+        ms2 = max_over_ranks(t2, world) / n2
+        out[f"pos{P}"] = {"tok_s": round(1000.0 / ms2, 1), "ms_per_step": round(ms2, 5)}
+        del dec
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_ours(args, rank, world, local):
@@ -576,6 +596,7 @@ def main():
     ap.add_argument("--prefill-reps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-tp", action="store_true", help="skip the tensor-parallel batch-1 leg at N > 1")
+    ap.add_argument("--tp-long", type=lambda s: [int(x) for x in s.split(",") if x], default=[8192])
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-ref-megakernel", action="store_true",
                     help="skip timing the reference megakernel built for sm_100a (oracle/_ref)")
