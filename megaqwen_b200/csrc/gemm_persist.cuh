@@ -35,10 +35,13 @@ struct PCfg {
     static constexpr int NB = (EPI == EPI_SILU_MUL) ? 2 : 1;          // B tiles per stage
     static constexpr int B_BYTES = BN * GEMM_BK * 2;                  // one B tile (BN rows x 64)
     static constexpr int STAGE = GEMM_TILE_BYTES + NB * B_BYTES;      // A tile (128 rows) + B tiles
-    static constexpr int NSTAGES = (6 * STAGE <= 200 * 1024) ? 6 : 4;
+    // EPI_QKV stages the cos / sin rows of a tile's 128 positions (64 KB) and
+    // keeps one ring stage fewer for them
+    static constexpr int ROPE_BYTES = EPI == 4 ? 2 * GEMM_BM * 128 * 2 : 0;
+    static constexpr int NSTAGES = EPI == 4 ? 3 : ((6 * STAGE <= 200 * 1024) ? 6 : 4);
     static constexpr int ACC_COLS = BN * NB;                          // one accumulator buffer
     static constexpr int TMEM_COLS = 2 * ACC_COLS;                    // double-buffered
-    static constexpr int SMEM = NSTAGES * STAGE + 1024 + 256;
+    static constexpr int SMEM = NSTAGES * STAGE + 1024 + 256 + ROPE_BYTES;
     static_assert(TMEM_COLS <= 512, "two accumulator buffers fit in TMEM");
     static_assert(BN * NB <= 256, "one MMA covers the stacked B tiles (N <= 256)");
 };
@@ -89,7 +92,11 @@ __device__ __forceinline__ uint4 pack8_bf16(const float* v) {
 // and v, to the cache.  map: 0 q, 1 k, 2 v; head within the map.  Every lane
 // of the warp calls it (the TMEM loads are warp-collective); lanes whose row
 // is past M store nothing.
-__device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, int map, int head, int row_in) {
+// cs / sn: this row's cos / sin table rows, staged in shared memory with the
+// 16-byte chunk c of the row stored at chunk c ^ sw (sw = row & 15), so that
+// the 8 lanes of a quarter warp (8 consecutive rows) read 8 different banks.
+__device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, int map, int head, int row_in,
+                                                 const __nv_bfloat16* cs, const __nv_bfloat16* sn, int sw) {
     const QkvPrefillEpi& e = a.qkv;
     const bool valid = row_in < a.M;
     const int row = valid ? row_in : 0;
@@ -132,8 +139,6 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
     }
     const float r = rsqrtf(ss / 128.f + 1e-6f);
     const __nv_bfloat16* nw = map == 0 ? e.q_norm : e.k_norm;
-    const __nv_bfloat16* cs = e.cos_table + (size_t)p * 128;
-    const __nv_bfloat16* sn = e.sin_table + (size_t)p * 128;
     const float osc = map == 0 ? e.q_scale : 1.f;
     // rotate-half pairs (d, d + 64): chunk c with chunk c + 64; weights, cos and
     // sin rows are read 8 bf16 at a time
@@ -146,8 +151,9 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
         for (int i = 0; i < 32; i += 8) {
             const int d = c + i;
             const uint4 w1 = *reinterpret_cast<const uint4*>(nw + d), w2 = *reinterpret_cast<const uint4*>(nw + d + 64);
-            const uint4 c1 = *reinterpret_cast<const uint4*>(cs + d), c2 = *reinterpret_cast<const uint4*>(cs + d + 64);
-            const uint4 s1 = *reinterpret_cast<const uint4*>(sn + d), s2 = *reinterpret_cast<const uint4*>(sn + d + 64);
+            const int k1 = ((d >> 3) ^ sw) << 3, k2 = (((d + 64) >> 3) ^ sw) << 3;
+            const uint4 c1 = *reinterpret_cast<const uint4*>(cs + k1), c2 = *reinterpret_cast<const uint4*>(cs + k2);
+            const uint4 s1 = *reinterpret_cast<const uint4*>(sn + k1), s2 = *reinterpret_cast<const uint4*>(sn + k2);
             const uint32_t w1v[4] = {w1.x, w1.y, w1.z, w1.w}, w2v[4] = {w2.x, w2.y, w2.z, w2.w};
             const uint32_t c1v[4] = {c1.x, c1.y, c1.z, c1.w}, c2v[4] = {c2.x, c2.y, c2.z, c2.w};
             const uint32_t s1v[4] = {s1.x, s1.y, s1.z, s1.w}, s2v[4] = {s2.x, s2.y, s2.z, s2.w};
@@ -193,6 +199,8 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     uint64_t* acce = accf + 2;                  // [2] epilogue -> MMA
     uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(acce + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+    // EPI_QKV: cos / sin rows of the tile's positions, [2 (cos, sin)][128 rows][128]
+    __nv_bfloat16* rope = reinterpret_cast<__nv_bfloat16*>(smem + Cfg::NSTAGES * Cfg::STAGE + 256);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ntiles = args.tiles_m * args.tiles_n;
@@ -314,7 +322,33 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(pp) + q));
                 }
             }
-            if (!bounded_wait(&accf[b], u & 1, args.timeout_cycles) || *abort_flag) {
+            if (EPI == EPI_QKV) {
+                // Stage the cos / sin rows of this quadrant's 32 positions while the
+                // MMAs run (warp half 0: cos, 1: sin; one 256-byte row per 16 lanes):
+                // one round of coalesced loads instead of dependent per-row loads in
+                // the epilogue.  The partner warp of the quadrant is done with the
+                // previous tile's rows at the first barrier.
+                named_bar_sync(1 + quad, 64);
+                const int mt = (t / args.tiles_n) * GEMM_BM;
+                const bool is_v = (t % args.tiles_n) >= args.nb0 + args.nb1;
+                if (!is_v) {
+                    const __nv_bfloat16* tab = half ? args.qkv.sin_table : args.qkv.cos_table;
+                    __nv_bfloat16* dst = rope + (size_t)(half * GEMM_BM + quad * 32) * 128;
+#pragma unroll 4
+                    for (int i = lane; i < 32 * 16; i += 32) {
+                        const int r = i >> 4, ch = i & 15;
+                        const int grow = mt + quad * 32 + r;
+                        const int gr = grow < args.M ? grow : 0;
+                        const int pp = args.qkv.start_pos + gr % args.qkv.S;
+                        *reinterpret_cast<uint4*>(dst + r * 128 + ((ch ^ (r & 15)) * 8)) =
+                            *reinterpret_cast<const uint4*>(tab + (size_t)pp * 128 + ch * 8);
+                    }
+                }
+            }
+            bool acc_ok = bounded_wait(&accf[b], u & 1, args.timeout_cycles) && !*abort_flag;
+            // EPI_QKV: the quadrant's two warps decide together (the barrier also publishes the staged rows)
+            if (EPI == EPI_QKV) acc_ok = !named_bar_or(1 + quad, 64, !acc_ok);
+            if (!acc_ok) {
                 if (lane == 0) atomicExch(args.err, 34);
                 *abort_flag = 1;
                 break;
@@ -335,11 +369,13 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     }
                 }
                 // one head per epilogue warp (BN = 256), or the two halves of one head
+                const __nv_bfloat16* cs = rope + (size_t)(quad * 32 + lane) * 128;
+                const __nv_bfloat16* sn = rope + (size_t)(GEMM_BM + quad * 32 + lane) * 128;
                 if (BN == 256) {
-                    qkv_row_epilogue(args, acc + half * 128, map, head * 2 + half, row);
+                    qkv_row_epilogue(args, acc + half * 128, map, head * 2 + half, row, cs, sn, lane & 15);
                 } else {
                     // BN = 128: the partner warp stays idle for this tile
-                    if (half == 0) qkv_row_epilogue(args, acc, map, head, row);
+                    if (half == 0) qkv_row_epilogue(args, acc, map, head, row, cs, sn, lane & 15);
                 }
             } else {
                 const int n0 = nt_all * BN + half * HB;
