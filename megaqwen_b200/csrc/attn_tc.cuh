@@ -56,6 +56,9 @@ constexpr uint32_t TM_O = 256, TM_P = 384;
 struct Args {
     __nv_bfloat16* O;       // [M, 2048] bf16, row m = b * S + s
     int S;                  // sequence length
+    // K is read straight from the layer's K cache (rows of 128): key s of kv head
+    // h of sequence b is row k_row0 + b * k_seq_rows + h * k_head_rows + s
+    long long k_row0, k_seq_rows, k_head_rows;
     int* err;
     long long timeout_cycles;
     unsigned long long* trace;   // optional: %globaltimer stamps of block (0,0,0), softmax warp 2, tiles < 32
@@ -84,7 +87,9 @@ __device__ __forceinline__ bool fa_wait(uint64_t* bar, uint32_t parity, long lon
     return true;
 }
 
-// tmQ: Qb [M, 2048]; tmK: Kb [M, 1024]; tmV: V^T [B * 8 * 128, ldv] (rows = (b * 8 + kvh) * 128 + d).
+// tmQ: Qb [M, 2048]; tmK: the K cache as rows of 128 (see Args); tmV: V^T [B * 8 * 128, ldv]
+// (rows = (b * 8 + kvh) * 128 + d).  Key rows past S (the last tile) hold other
+// cache rows or TMA zero fill; the softmax masks them.
 __global__ void __launch_bounds__(THREADS, 1)
 fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
              const __grid_constant__ CUtensorMap tmV, const Args args) {
@@ -162,8 +167,9 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                 if (*abort_flag) break;
                 uint8_t* kd = smem + SM_K + st * TILE;
                 mbar_arrive_expect_tx(&k_full[st], TILE);
-                tma_load_2d(kd, &tmK, kvh * HD, row0 + j * BK, &k_full[st]);
-                tma_load_2d(kd + ATOM, &tmK, kvh * HD + 64, row0 + j * BK, &k_full[st]);
+                const int krow = (int)(args.k_row0 + b * args.k_seq_rows + kvh * args.k_head_rows) + j * BK;
+                tma_load_2d(kd, &tmK, 0, krow, &k_full[st]);
+                tma_load_2d(kd + ATOM, &tmK, 64, krow, &k_full[st]);
             }
         } else if (lane == 1) {
             const int vrow = (b * 8 + kvh) * HD;

@@ -16,7 +16,7 @@
 // EPI_QKV (prefill QKV projection): each 128 columns of a tile are one head.  q and k
 // heads get RMSNorm over the head (x norm weight) and rotate-half RoPE at the
 // row's position, in the thread that owns the row (no cross-thread traffic);
-// q goes to Qb, k and v to Kb / Vb and to the sequence's K/V cache (bf16).
+// q goes to Qb, k and v to the sequence's K/V cache (bf16), v also transposed.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -52,8 +52,6 @@ struct QkvPrefillEpi {
     const __nv_bfloat16* cos_table;   // [max_seq, 128]
     const __nv_bfloat16* sin_table;
     __nv_bfloat16* Qb;                // [M, 2048]
-    __nv_bfloat16* Kb;                // [M, 1024]
-    __nv_bfloat16* Vb;                // [M, 1024]
     __nv_bfloat16* k_cache;           // layer base of sequence 0: [8, max_seq, 128]
     __nv_bfloat16* v_cache;
     long long cache_seq_stride;       // elements between sequences' caches
@@ -101,8 +99,9 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
     const bool valid = row_in < a.M;
     const int row = valid ? row_in : 0;
     const int b = row / e.S, p = e.start_pos + (row - b * e.S);
-    __nv_bfloat16* dst = map == 0 ? e.Qb + (size_t)row * 2048 + head * 128
-                                  : (map == 1 ? e.Kb : e.Vb) + (size_t)row * 1024 + head * 128;
+    // q goes to Qb; k and v only to the cache (the attention reads K from the
+    // cache and V from V^T)
+    __nv_bfloat16* dst = map == 0 ? e.Qb + (size_t)row * 2048 + head * 128 : nullptr;
     __nv_bfloat16* cache = map == 0 ? nullptr
                                     : (map == 1 ? e.k_cache : e.v_cache) + b * e.cache_seq_stride +
                                           ((size_t)head * e.max_seq + p) * 128;
@@ -118,7 +117,6 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
 #pragma unroll
                 for (int i = 0; i < 32; i += 8) {
                     const uint4 pk = pack8_bf16(v + i);
-                    *reinterpret_cast<uint4*>(dst + c + i) = pk;
                     *reinterpret_cast<uint4*>(cache + c + i) = pk;
                 }
                 if (vt) {
@@ -174,12 +172,9 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
             }
             if (valid) {
                 const uint4 p1 = pack8_bf16(o1), p2 = pack8_bf16(o2);
-                *reinterpret_cast<uint4*>(dst + d) = p1;
-                *reinterpret_cast<uint4*>(dst + d + 64) = p2;
-                if (map == 1) {
-                    *reinterpret_cast<uint4*>(cache + d) = p1;
-                    *reinterpret_cast<uint4*>(cache + d + 64) = p2;
-                }
+                __nv_bfloat16* out = map == 0 ? dst : cache;
+                *reinterpret_cast<uint4*>(out + d) = p1;
+                *reinterpret_cast<uint4*>(out + d + 64) = p2;
             }
         }
     }

@@ -160,7 +160,7 @@ namespace {
 unsigned long long* g_fa_trace = nullptr;
 
 struct PrefillLayout {
-    size_t X, Xn, Qb, Kb, Vb, Vt, Ob, act, lastn, logits, err, total;
+    size_t X, Xn, Qb, Vt, Ob, act, lastn, logits, err, total;
 };
 
 PrefillLayout prefill_layout(int B, int S) {
@@ -171,8 +171,6 @@ PrefillLayout prefill_layout(int B, int S) {
     L.X = take(M * 1024 * 4);
     L.Xn = take(M * 1024 * 2);
     L.Qb = take(M * 2048 * 2);
-    L.Kb = take(M * 1024 * 2);
-    L.Vb = take(M * 1024 * 2);
     L.Vt = take((size_t)B * 8 * 128 * ((S + 7) / 8 * 8) * 2);   // V^T per (sequence, kv head), rows padded to 8
     L.Ob = take(M * 2048 * 2);
     L.act = take(M * 3072 * 2);
@@ -204,8 +202,6 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
     float* X = (float*)(ws + L.X);
     pf::bf16* Xn = (pf::bf16*)(ws + L.Xn);
     pf::bf16* Qb = (pf::bf16*)(ws + L.Qb);
-    pf::bf16* Kb = (pf::bf16*)(ws + L.Kb);
-    pf::bf16* Vb = (pf::bf16*)(ws + L.Vb);
     pf::bf16* Ob = (pf::bf16*)(ws + L.Ob);
     pf::bf16* act = (pf::bf16*)(ws + L.act);
     pf::bf16* lastn = (pf::bf16*)(ws + L.lastn);
@@ -225,11 +221,17 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             fa_configured[dev] = true;
         }
     }
-    // attention operands: Q [M, 2048], K [M, 1024] and V^T [B * 8 * 128, ldvt] (zero padding past S)
+    // attention operands: Q [M, 2048], K straight from the K cache (rows of 128 over all
+    // sequences and layers) and V^T [B * 8 * 128, ldvt] (zero padding past S)
     pf::bf16* Vt = (pf::bf16*)(ws + L.Vt);
     const int ldvt = (S + 7) / 8 * 8;
+    if (p->cache_seq_stride % MQ_HEAD_DIM != 0) return MQ_ERR_INVALID_ARGUMENT;
+    const long long seq_rows = p->cache_seq_stride / MQ_HEAD_DIM;
+    const long long head_rows = p->max_seq_len;
+    const long long cache_rows = (long long)(B - 1) * seq_rows + (long long)p->num_layers * MQ_NUM_KV_HEADS * head_rows;
     CUtensorMap tmQ, tmK, tmV;
-    if (!make_tmap(&tmQ, Qb, (uint64_t)M, 2048, 2048, fa::BQ) || !make_tmap(&tmK, Kb, (uint64_t)M, 1024, 1024, fa::BK) ||
+    if (!make_tmap(&tmQ, Qb, (uint64_t)M, 2048, 2048, fa::BQ) ||
+        !make_tmap(&tmK, p->k_cache, (uint64_t)cache_rows, MQ_HEAD_DIM, MQ_HEAD_DIM, fa::BK) ||
         !make_tmap(&tmV, Vt, (uint64_t)B * 8 * 128, (uint64_t)ldvt, (uint64_t)ldvt, 128))
         return MQ_ERR_CUDA;
     if (ldvt != S && cudaMemsetAsync(Vt, 0, (size_t)B * 8 * 128 * ldvt * 2, st) != cudaSuccess) return MQ_ERR_CUDA;
@@ -245,8 +247,6 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             e.cos_table = (const pf::bf16*)p->cos_table;
             e.sin_table = (const pf::bf16*)p->sin_table;
             e.Qb = Qb;
-            e.Kb = Kb;
-            e.Vb = Vb;
             const size_t layer_off = (size_t)l * MQ_NUM_KV_HEADS * p->max_seq_len * MQ_HEAD_DIM;
             e.k_cache = (pf::bf16*)p->k_cache + layer_off;
             e.v_cache = (pf::bf16*)p->v_cache + layer_off;
@@ -265,6 +265,9 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             fa::Args fa_args;
             fa_args.O = Ob;
             fa_args.S = S;
+            fa_args.k_row0 = (long long)l * MQ_NUM_KV_HEADS * head_rows;
+            fa_args.k_seq_rows = seq_rows;
+            fa_args.k_head_rows = head_rows;
             fa_args.err = err;
             fa_args.timeout_cycles = 4000000000ll;
             fa_args.trace = nullptr;
