@@ -34,7 +34,7 @@ EXT = PKG / ("_C" + sysconfig.get_config_var("EXT_SUFFIX"))
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_SOURCES = ["decode.cu", "prefill.cu", "decode_batch.cu"]
-CUDA_HEADERS = ["mq_ptx.cuh", "mq_tc.cuh", "gemm_tc.cuh", "gemm_small.cuh", "gemm_persist.cuh", "attn_tc.cuh", "prefill_kernels.cuh", "attn_fa.cuh"]
+CUDA_HEADERS = ["mq_ptx.cuh", "mq_tc.cuh", "gemm_tc.cuh", "gemm_small.cuh", "gemm_persist.cuh", "gemm_pair.cuh", "attn_tc.cuh", "prefill_kernels.cuh", "attn_fa.cuh"]
 
 
 def _nvcc() -> str:

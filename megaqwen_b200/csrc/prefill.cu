@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -12,6 +13,7 @@
 
 #include "gemm_tc.cuh"
 #include "gemm_persist.cuh"
+#include "gemm_pair.cuh"
 #include "megaqwen_b200.h"
 
 namespace mq {
@@ -113,9 +115,67 @@ int launch_persist(const void* A, int lda, const void* const* Bm, const int* Nma
     return launch_persist_bn<EPI, 128>(A, lda, Bm, Nmap, nmaps, ldb, C, ldc, M, K, qkv, err, stream);
 }
 
+// The CTA-pair GEMM (gemm_pair.cuh) for EPI_ADD_F32 / EPI_SILU_MUL: 256-row
+// pair tiles, launched as clusters of two, one pair per two SMs.
+template <int EPI>
+int launch_pair(const void* A, int lda, const void* B, const void* B2, int ldb, void* C, int ldc, int M, int N, int K,
+                int* err, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return MQ_ERR_CUDA;
+    if (dev < 64 && !configured[dev]) {
+        if (cudaFuncSetAttribute(gemm_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, PAIR_SMEM) !=
+            cudaSuccess)
+            return MQ_ERR_CUDA;
+        configured[dev] = true;
+    }
+    CUtensorMap ta, tb0, tb1;
+    if (!make_tmap(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, GEMM_BM) ||
+        !make_tmap(&tb0, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128) ||
+        !make_tmap(&tb1, B2 ? B2 : B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 128))
+        return MQ_ERR_CUDA;
+    PArgs a = {};
+    a.C = C;
+    a.ldc = ldc;
+    a.M = M;
+    a.K = K;
+    a.tiles_m = (M + 255) / 256;
+    a.tiles_n = EPI == EPI_SILU_MUL ? N / 128 : N / 256;
+    a.err = err;
+    a.timeout_cycles = 4000000000ll;
+    const int ntiles = a.tiles_m * a.tiles_n;
+    const int pairs = std::min(ntiles, num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * pairs);
+    cfg.blockDim = dim3(P_THREADS);
+    cfg.dynamicSmemBytes = PAIR_SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb0, tb1, a);
+    return e == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+}
+
+// The pair GEMM serves the residual-add GEMMs once their 256 x 256 pair tiles
+// fill every SM pair twice (B = 8 x 2048 prompts): 101.7 against 104.5 us per
+// launch.  Gate/up stays on the one-CTA kernel, where the pair version measured
+// 177 against 173 us (B = 8) and 33.5 against 32 us (B = 1).
+bool use_pair(int epi, int M, int N) {
+    if (epi == EPI_ADD_F32 && N % 256 == 0) return (long long)((M + 255) / 256) * (N / 256) >= num_sms();
+    return false;
+}
+
 template <int EPI>
 int launch_gemm(const void* A, int lda, const void* B, int ldb, const void* B2, void* C, int ldc, int M, int N,
                 int K, int* err, cudaStream_t stream) {
+    if ((EPI == EPI_ADD_F32 || EPI == EPI_SILU_MUL) && use_pair(EPI, M, N))
+        return launch_pair<EPI == EPI_SILU_MUL ? EPI_SILU_MUL : EPI_ADD_F32>(A, lda, B, B2, ldb, C, ldc, M, N, K, err,
+                                                                          stream);
     const void* Bm[2] = {B, B2 ? B2 : B};
     const int Nm[2] = {N, N};
     return launch_persist<EPI>(A, lda, Bm, Nm, EPI == EPI_SILU_MUL ? 2 : 1, ldb, C, ldc, M, K, nullptr, err, stream);

@@ -70,3 +70,34 @@ def test_gemm_residual_add_and_gate_up():
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     _gemm(lib, A, B, out, 3)
     assert (out.float() - gte).abs().max().item() <= 1e-2 * gte.abs().max().item()
+
+
+@pytest.mark.parametrize("M,N,K", [(9856, 1024, 2048), (16384, 1024, 3072)])
+def test_pair_gemm_residual_add(M, N, K):
+    """Shapes with enough 256 x 256 pair tiles for the CTA-pair (cta_group::2)
+    GEMM: C += A . B^T against torch, ragged M included."""
+    lib = _lib()
+    g = torch.Generator(device="cuda").manual_seed(M + K)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    R = torch.randn(M, N, device="cuda", generator=g)
+    C = R.clone()
+    _gemm(lib, A, B, C, 1)
+    ref = R + A.float() @ B.float().T
+    assert (C - ref).abs().max().item() <= 1e-4 * ref.abs().max().item()
+
+
+@pytest.mark.parametrize("M", [2048, 2000, 16384])
+def test_gate_up_large(M):
+    """gate/up + SiLU*mul at the prefill shapes (B = 1 and 8 x 2048 prompts,
+    ragged M) against torch."""
+    lib = _lib()
+    N, K = 3072, 1024
+    g = torch.Generator(device="cuda").manual_seed(M)
+    A = torch.randn(M, K, device="cuda", generator=g).to(torch.bfloat16)
+    B = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    B2 = (torch.randn(N, K, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    act = torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16)
+    _gemm(lib, A, B, act, 2, B2=B2)
+    ref = torch.nn.functional.silu(A.float() @ B.float().T) * (A.float() @ B2.float().T)
+    assert (act.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
