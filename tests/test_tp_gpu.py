@@ -1,7 +1,7 @@
-"""KV-head tensor-parallel decode on 2 GPUs (MegakernelTPDecoder, one process
-per GPU, the kernel exchanging partials over NVLink) against the CPU oracle,
-and failure detection across ranks without a GPU fault.  Skipped on hosts
-with fewer than two GPUs.
+"""KV-head tensor-parallel decode on 2, 4 and 8 GPUs (MegakernelTPDecoder, one
+process per GPU, the kernel exchanging partials over NVLink) against the CPU
+oracle, and failure detection across ranks without a GPU fault.  Each case is
+skipped on hosts with fewer GPUs than ranks.
 
 Bar as for the single-GPU decode: per-step logits max-abs <= 3e-2 and cosine
 >= 0.9995 against the oracle, greedy tokens identical.  Each rank writes the
@@ -117,26 +117,26 @@ def _rank_timeout(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def _need_two():
+def _need(n):
     assert torch.cuda.is_available(), "GPU tests need a CUDA device"
-    if torch.cuda.device_count() < 2:
-        pytest.skip("tensor-parallel decode needs 2 GPUs")
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"tensor-parallel decode over {n} ranks needs {n} GPUs")
 
 
-@pytest.mark.parametrize("num_layers,steps", [(2, 24), (28, 24)])
-def test_tp2_decode_matches_oracle(num_layers, steps):
-    _need_two()
+@pytest.mark.parametrize("world,num_layers,steps", [(2, 2, 24), (2, 28, 24), (4, 28, 16), (8, 28, 16)])
+def test_tp_decode_matches_oracle(world, num_layers, steps):
+    _need(world)
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
-    mp.start_processes(_rank, args=(2, _free_port(), num_layers, steps, out), nprocs=2, join=True,
+    mp.start_processes(_rank, args=(world, _free_port(), num_layers, steps, out), nprocs=world, join=True,
                        start_method="spawn")
-    for r in range(2):
+    for r in range(world):
         assert out[r][0] == "ok", out[r][1]
-    print(f"TP-2 L={num_layers}: worst logits max-abs {out[0][1]:.3e}")
+    print(f"TP-{world} L={num_layers}: worst logits max-abs {out[0][1]:.3e}")
 
 
 def test_tp2_wait_timeout_is_reported_on_every_rank_and_recoverable():
-    _need_two()
+    _need(2)
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     mp.start_processes(_rank_timeout, args=(2, _free_port(), out), nprocs=2, join=True, start_method="spawn")
