@@ -473,6 +473,7 @@ def run_ours(args, rank, world, local):
             dec.decode_step_async(tok_buf.data_ptr(), tok_buf.data_ptr())
         dec.check()
         p_first = dec.position()
+        tok_first = int(tok_buf.item())
         barrier(world)
         clk.mark(True)
         total_ms = time_device_steps(dec, tok_buf, args.steps)
@@ -486,10 +487,13 @@ def run_ours(args, rank, world, local):
         p_mid = p_first + args.steps // 2
         achieved = bytes_per_token(p_mid) / (launch_ms / 1000.0) / 1e9
 
-        # --- e2e through the public API: host token in, host token out each step ---
+        # --- e2e through the public API: host token in, host token out each step,
+        # over the same positions and tokens as the timed region ---
         cur = int(tok_buf.item())
         for _ in range(3):
             cur = dec.decode_step(cur)
+        dec.set_position(p_first)
+        cur = tok_first
         barrier(world)
         t0 = time.perf_counter()
         e2e_steps = args.steps
@@ -566,7 +570,8 @@ def run_ours(args, rank, world, local):
                          "peak_kind": hbm_kind, "bytes_per_launch": bytes_per_token(p_mid),
                          "launch_ms": round(launch_ms, 5)},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 16,
-                    "d2h_path": "token, error, info, seq written by the kernel to mapped pinned host memory"},
+                    "d2h_path": "token, error, info, seq written by the kernel to mapped pinned host memory",
+                    "positions": f"{p_first}..{p_first + args.steps - 1} (the timed region's positions and tokens)"},
             "clocks": clk.summary(),
             "positions": sweep,
             "prefill": sweep_prefill,
