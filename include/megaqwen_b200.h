@@ -177,6 +177,11 @@ size_t mq_decode_workspace_bytes(void);
 /* Zero a workspace (stream-ordered).  Needed once before first use and after
  * any call that returned an error. */
 int mq_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream);
+/* Set the step counter kept in a workspace (stream-ordered).  Every step tags
+ * its inter-CTA handoff words with this counter, which wraps to 0 after
+ * 2^25 - 1; this entry point lets tests and diagnostics run steps across the
+ * wrap.  epoch must be below 2^25. */
+int mq_decode_workspace_set_epoch(void* workspace, uint32_t epoch, cudaStream_t stream);
 /* Launch one decode step.  Host-side argument checks return an error code
  * without launching; device-side failures land in the workspace error word. */
 int mq_decode(const mq_decode_params* params, cudaStream_t stream);

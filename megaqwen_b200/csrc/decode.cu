@@ -1422,6 +1422,14 @@ struct Consumer {
                 C->last_token = tok;
                 C->last_position = S.pos;
                 if (P.position_ptr) *P.position_ptr = S.pos + 1;
+                // The tags of this step's words are (epoch + 1) << 6 | layer, so the
+                // counter wraps after 2^25 steps (the tag stays within 32 bits).  A
+                // wrap is harmless: a handoff slot read in a step is written in that
+                // step, and the word it held before came from the previous step (a
+                // different epoch) or, for attention partials of a chunk index the
+                // previous step did not use, from an older step, which would have to be
+                // exactly 2^25 steps old to match.  A failed step leaves the epoch as
+                // it is and the host zeroes the whole workspace before the next one.
                 C->epoch = (C->epoch + 1u) & ((1u << 25) - 1u);
                 __threadfence();
             }
@@ -1785,6 +1793,18 @@ int mq_decode_workspace_init(void* workspace, size_t bytes, cudaStream_t stream)
 }
 
 int mq_decode(const mq_decode_params* params, cudaStream_t stream) { return launch(params, stream); }
+
+namespace {
+__global__ void set_epoch_kernel(mq::Control* c, uint32_t e) { c->epoch = e; }
+}  // namespace
+
+int mq_decode_workspace_set_epoch(void* workspace, uint32_t epoch, cudaStream_t stream) {
+    if (!workspace) return MQ_ERR_WORKSPACE;
+    if (epoch >= (1u << 25)) return MQ_ERR_INVALID_ARGUMENT;
+    set_epoch_kernel<<<1, 1, 0, stream>>>(reinterpret_cast<mq::Control*>(workspace), epoch);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MQ_OK : cuda_fail(e, "set_epoch_kernel");
+}
 
 }  // extern "C"
 

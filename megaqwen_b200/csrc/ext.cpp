@@ -200,6 +200,13 @@ public:
     void set_attn_chunk(int n) { attn_chunk_ = n; }
     void set_timeout_ns(long long t) { timeout_ns_ = t; }
     void set_inject_skip_cta(int c) { inject_skip_cta_ = c; }
+    // Step counter of the handoff tags (wraps at 2^25): lets tests run across the wrap.
+    void set_step_epoch(int64_t e) {
+        c10::cuda::CUDAGuard guard(device_);
+        cudaStream_t stream = c10::cuda::getCurrentCUDAStream(device_.index()).stream();
+        int rc = mq_decode_workspace_set_epoch(workspace_.data_ptr(), (uint32_t)e, stream);
+        if (rc) raise_engine(rc, 0, "set_step_epoch");
+    }
     // Profiling: device int64 buffer of num_ctas * 512 timestamps, or 0 to disable.
     void set_trace(int64_t ptr) { trace_ = reinterpret_cast<unsigned long long*>(ptr); }
     int num_ctas() const { return num_ctas_ > 0 ? num_ctas_ : mq_decode_default_ctas(); }
@@ -955,7 +962,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         .def("set_attn_chunk", &MegakernelDecoder::set_attn_chunk)
         .def("set_timeout_ns", &MegakernelDecoder::set_timeout_ns)
         .def("set_inject_skip_cta", &MegakernelDecoder::set_inject_skip_cta)
-        .def("set_trace", &MegakernelDecoder::set_trace);
+        .def("set_trace", &MegakernelDecoder::set_trace)
+        .def("set_step_epoch", &MegakernelDecoder::set_step_epoch);
     py::class_<MegakernelTPDecoder, MegakernelDecoder>(m, "MegakernelTPDecoder")
         .def(py::init<torch::Tensor, std::vector<torch::Tensor>, torch::Tensor, torch::Tensor, torch::Tensor,
                       torch::Tensor, int, int, int, int>(),

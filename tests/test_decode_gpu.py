@@ -199,6 +199,27 @@ def test_prefill_classes_and_position_semantics():
     assert dec.position() == 0 and int(dec.get_k_cache().abs().sum().item()) == 0
 
 
+def test_step_counter_wrap_does_not_change_tokens():
+    """The handoff words carry the step counter (25 bits, wraps to 0); steps
+    run across the wrap give the same greedy tokens as steps far from it."""
+    from megaqwen_b200.weights import seeded_prompt
+    prompt = seeded_prompt(8).tolist()
+
+    def run(epoch):
+        dec = make_decoder(28, 64)
+        if epoch is not None:
+            dec.set_step_epoch(epoch)
+        out, cur = [], prompt[0]
+        for i in range(len(prompt) + 8):
+            tok = dec.decode_step(cur)
+            out.append(tok)
+            cur = prompt[i + 1] if i + 1 < len(prompt) else tok
+        return out
+
+    ref = run(None)
+    assert run((1 << 25) - 5) == ref
+
+
 def test_position_and_token_bounds():
     dec = make_decoder(1, 4)
     for t in range(4):
