@@ -125,7 +125,19 @@ __global__ void __launch_bounds__(128, 4) attn_unit_kernel(const float* __restri
     // Each warp loads one 16-position group at a time straight into registers;
     // the latency is covered by the other resident warps (4+ CTAs per SM at
     // <= 128 registers) rather than by a second register buffer.
+    // L2 prefetch of this warp's K/V rows two groups ahead (one bulk prefetch per
+    // matrix and group, issued by lane 0), so the register loads hit L2
+    auto prefetch = [&](int grp) {
+        if (lane == 0 && grp < ngroups) {
+            const int r0 = 16 * grp, rows = min(16, n - r0);
+            bulk_prefetch_l2(kb + (size_t)r0 * D, (uint32_t)(rows * D * 2));
+            bulk_prefetch_l2(vb + (size_t)r0 * D, (uint32_t)(rows * D * 2));
+        }
+    };
+    prefetch(warp);
+    prefetch(warp + 4);
     for (int grp = warp; grp < ngroups; grp += 4) {
+        prefetch(grp + 8);
         load(grp, kr, vr);
         // S^T[16 positions][8 heads]
         float s[4] = {0.f, 0.f, 0.f, 0.f};
