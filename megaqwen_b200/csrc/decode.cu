@@ -19,8 +19,10 @@
 //  * RMSNorms are recomputed redundantly by every CTA from the polled vector.
 //  * Attention is split-K flash decoding: 8 kv heads x C position chunks, one
 //    work unit per CTA, each unit serving both q heads of its kv head (every
-//    K/V byte read once).  With C > 1 the last-arriving unit combines the
-//    partial (max, sum, acc) triples.
+//    K/V byte read once).  Units of up to 128 positions use fp32 dot products
+//    spread over all 15 warps; longer units the tensor cores (mma.sync).
+//    With C > 1, unit 0 of each kv head combines the partial (max, sum, acc)
+//    triples.
 //  * The LM head is fused: each CTA takes a slice of vocabulary rows, keeps a
 //    running (value, index) best, publishes it with one 64-bit atomicMax, and
 //    the last CTA to arrive writes the token.
@@ -84,6 +86,11 @@ static_assert(MV_GROUP * QKV_TILE <= MV_Q * NCW && MV_GROUP * LM_TILE <= MV_Q * 
               "a group's rows fit MV_Q rows per warp (O and down stages hold at most NCW rows)");
 static_assert(MV_GROUP < NSTAGES, "the producer can fill a whole group");
 constexpr int KV_TILE = STAGE_BYTES / (2 * D * 2);   // 64 positions (K and V)
+// Units of up to two 64-position tiles (every unit up to p = 2303) run the
+// fp32 attention path; longer ones the tensor-core path (measured: fp32 for
+// all units was 2 % faster at p = 2048 but 1.4 % slower at 8192 and 5 % at
+// 32768).
+constexpr int ATTN_FP32_MAX_TILES = 2;
 static_assert(KV_TILE == 64 && 4 * MV_GROUP <= NCW, "attention: 4 groups of 16 positions per tile, one warp each");
 static_assert(QKV_TILE <= NCW && O_TILE <= NCW && GU_TILE <= NCW && DOWN_TILE <= NCW && LM_TILE <= NCW,
               "one consumer warp per row of a tile");
@@ -908,33 +915,10 @@ struct Consumer {
     __device__ __forceinline__ bool run(int phase, int l) {
         if (!begin<KIND>(phase, l)) return false;
         if (KIND == 1) {
-            AttnState a;
-            const float* qn = sm<float>(SM_QN);
-            const float sc = P.attn_scale * 1.4426950408889634f;   // log2 domain
-            uint32_t* qbs = sm<uint32_t>(SM_QKVRAW);
-            // word w = (k-step * 32 + lane') * 2 + j of the B fragments, one or two per thread;
-            // column g' = lane' / 4: head g' & 1, hi (g' < 2) or remainder (g' < 4), else 0
-            for (int w = ct; w < 512; w += NCT) {
-                const int jj = w & 1, lw = (w >> 1) & 31, ks = w >> 6;
-                const int gw = lw >> 2, tw = lw & 3;
-                const int d0 = 32 * (ks >> 1) + 8 * tw + 4 * (ks & 1) + 2 * jj;
-                const float* q = qn + (gw & 1) * D;
-                const float x0 = q[d0] * sc, x1 = q[d0 + 1] * sc;
-                const float h0 = bf16_round(x0), h1 = bf16_round(x1);
-                qbs[w] = gw < 2 ? pack2_bf16(h0, h1) : gw < 4 ? pack2_bf16(x0 - h0, x1 - h1) : 0u;
-            }
-            attn_stamp(l, 0);
-            named_bar_sync(BAR_CONSUMERS, NCT);
-#pragma unroll
-            for (int u = 0; u < 4; ++u)
-#pragma unroll
-                for (int qq = 0; qq < 2; ++qq) a.o[u][qq][0] = a.o[u][qq][1] = a.o[u][qq][2] = a.o[u][qq][3] = 0.f;
-            a.m[0] = a.m[1] = -INFINITY;
-            a.l[0] = a.l[1] = 0.f;
-            attn_stamp(l, 1);
-            attn_phase(a, l);
+            if (S.kv_e - S.kv_s <= ATTN_FP32_MAX_TILES * KV_TILE) attn_fp32(l);
+            else attn_long(l);
             attn_stamp(l, 2);
-            end_attn(a, l);
+            finish_attn(l);
             attn_stamp(l, 4);
             return true;
         }
@@ -1223,6 +1207,136 @@ struct Consumer {
             ml[warp * 4 + 0] = a.m[0]; ml[warp * 4 + 1] = a.l[0];
             ml[warp * 4 + 2] = a.m[1]; ml[warp * 4 + 3] = a.l[1];
         }
+    }
+
+    // A unit of more than KV_TILE cached positions: the tensor-core path
+    // (mma.sync m16n8k16 over 16-position groups, q and p as bf16 hi + lo).
+    __device__ __forceinline__ void attn_long(int l) {
+        AttnState a;
+        const float* qn = sm<float>(SM_QN);
+        const float sc = P.attn_scale * 1.4426950408889634f;   // log2 domain
+        uint32_t* qbs = sm<uint32_t>(SM_QKVRAW);
+        // word w = (k-step * 32 + lane') * 2 + j of the B fragments, one or two per thread;
+        // column g' = lane' / 4: head g' & 1, hi (g' < 2) or remainder (g' < 4), else 0
+        for (int w = ct; w < 512; w += NCT) {
+            const int jj = w & 1, lw = (w >> 1) & 31, ks = w >> 6;
+            const int gw = lw >> 2, tw = lw & 3;
+            const int d0 = 32 * (ks >> 1) + 8 * tw + 4 * (ks & 1) + 2 * jj;
+            const float* q = qn + (gw & 1) * D;
+            const float x0 = q[d0] * sc, x1 = q[d0 + 1] * sc;
+            const float h0 = bf16_round(x0), h1 = bf16_round(x1);
+            qbs[w] = gw < 2 ? pack2_bf16(h0, h1) : gw < 4 ? pack2_bf16(x0 - h0, x1 - h1) : 0u;
+        }
+        attn_stamp(l, 0);
+        named_bar_sync(BAR_CONSUMERS, NCT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int qq = 0; qq < 2; ++qq) a.o[u][qq][0] = a.o[u][qq][1] = a.o[u][qq][2] = a.o[u][qq][3] = 0.f;
+        a.m[0] = a.m[1] = -INFINITY;
+        a.l[0] = a.l[1] = 0.f;
+        attn_stamp(l, 1);
+        attn_phase(a, l);
+        end_attn(a, l);
+    }
+
+    // Attention of one unit in plain fp32, for units of up to
+    // ATTN_FP32_MAX_TILES staged tiles: warp w takes positions w, w + 15, ..
+    // of each 64-position tile, so all 15 warps work and no q fragments,
+    // transposes or fragment reductions are needed.  Lane owns head dims
+    // 4 lane .. 4 lane + 3 of both q heads; scores are in the log2 domain like
+    // the tensor-core path's, and a warp's (max, sum, acc) is carried across
+    // tiles with the usual online-softmax rescale.  The warp's state goes to
+    // its entry slot for finish_attn.
+    __device__ __forceinline__ void attn_fp32(int l) {
+        constexpr int RPW = (KV_TILE + NCW - 1) / NCW;   // positions per warp and tile (5)
+        float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);
+        float* ml = reinterpret_cast<float*>(g_smem + SM_ML);
+        const float sc = P.attn_scale * 1.4426950408889634f;
+        const float4 qa = *reinterpret_cast<const float4*>(sm<float>(SM_QN) + 4 * lane);
+        const float4 qb = *reinterpret_cast<const float4*>(sm<float>(SM_QN) + D + 4 * lane);
+        const int total = S.kv_e - S.kv_s;
+        float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int t0 = 0; t0 < total; t0 += KV_TILE) {
+            const int nrows = min(total - t0, KV_TILE);
+            const bool got = wait_full(n % NSTAGES, (n / NSTAGES) & 1u, PH_ATTN, l);
+            if (got && warp < nrows) {
+                const uint8_t* kb = g_smem + SM_STAGES + (n % NSTAGES) * STAGE_BYTES;
+                const uint8_t* vb = kb + nrows * D * 2;
+                float s0[RPW], s1[RPW];
+#pragma unroll
+                for (int i = 0; i < RPW; ++i) {
+                    const int r = warp + NCW * i;
+                    s0[i] = s1[i] = 0.f;
+                    if (r < nrows) {
+                        const uint2 kw = *reinterpret_cast<const uint2*>(kb + r * (D * 2) + 8 * lane);
+                        const float k0 = bf16lo(kw.x), k1 = bf16hi(kw.x), k2 = bf16lo(kw.y), k3 = bf16hi(kw.y);
+                        s0[i] = qa.x * k0 + qa.y * k1 + qa.z * k2 + qa.w * k3;
+                        s1[i] = qb.x * k0 + qb.y * k1 + qb.z * k2 + qb.w * k3;
+                    }
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                    for (int i = 0; i < RPW; ++i) {
+                        s0[i] += __shfl_xor_sync(0xffffffffu, s0[i], o);
+                        s1[i] += __shfl_xor_sync(0xffffffffu, s1[i], o);
+                    }
+                float t0m = m0, t1m = m1;
+#pragma unroll
+                for (int i = 0; i < RPW; ++i) {
+                    if (warp + NCW * i < nrows) {
+                        s0[i] *= sc;
+                        s1[i] *= sc;
+                        t0m = fmaxf(t0m, s0[i]);
+                        t1m = fmaxf(t1m, s1[i]);
+                    }
+                }
+                const float c0 = exp2f(m0 - t0m), c1 = exp2f(m1 - t1m);   // 0 on the first tile
+                m0 = t0m;
+                m1 = t1m;
+                l0 *= c0;
+                l1 *= c1;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    a0[j] *= c0;
+                    a1[j] *= c1;
+                }
+#pragma unroll
+                for (int i = 0; i < RPW; ++i) {
+                    const int r = warp + NCW * i;
+                    if (r < nrows) {
+                        const float e0 = exp2f(s0[i] - m0), e1 = exp2f(s1[i] - m1);
+                        l0 += e0;
+                        l1 += e1;
+                        const uint2 vw = *reinterpret_cast<const uint2*>(vb + r * (D * 2) + 8 * lane);
+                        const float v[4] = {bf16lo(vw.x), bf16hi(vw.x), bf16lo(vw.y), bf16hi(vw.y)};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            a0[j] = fmaf(e0, v[j], a0[j]);
+                            a1[j] = fmaf(e1, v[j], a1[j]);
+                        }
+                    }
+                }
+            }
+            release(n % NSTAGES);
+            n += 1;
+        }
+        *reinterpret_cast<float4*>(acc + (warp * 2 + 0) * D + 4 * lane) = make_float4(a0[0], a0[1], a0[2], a0[3]);
+        *reinterpret_cast<float4*>(acc + (warp * 2 + 1) * D + 4 * lane) = make_float4(a1[0], a1[1], a1[2], a1[3]);
+        if (lane == 0) {
+            ml[warp * 4 + 0] = m0; ml[warp * 4 + 1] = l0;
+            ml[warp * 4 + 2] = m1; ml[warp * 4 + 3] = l1;
+        }
+    }
+
+    // Merge of the unit's warp entries (+ the current position), then the
+    // split-K publish / combine (both attention paths).
+    __device__ __forceinline__ void finish_attn(int l) {
+        float* acc = reinterpret_cast<float*>(g_smem + SM_ACC);   // [16][2][128]
+        float* ml = reinterpret_cast<float*>(g_smem + SM_ML);     // [16][2][2]
         if (warp == NCW - 1) {
             // entry NCW: the current position (last unit only), fp32 q.k of the
             // bf16-rounded k/v held in shared memory
