@@ -35,10 +35,10 @@ KV_BYTES_PER_POS = 114_688              # K+V, all layers, one position (bf16)
 # DRAM bytes (read + write) per decode_step_kernel launch at position 19: the
 # mean of three launches captured with ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum, one pass, --clock-control none) on 2026-12-02 from the
-# tree of the tensor-parallel decode commit; traffic / algorithmic bytes =
-# 1.0023.  DRAM traffic tracks the algorithmic bytes, so the bench scales it to
+# tree of the fp32 short-unit attention commit; traffic / algorithmic bytes =
+# 1.0021.  DRAM traffic tracks the algorithmic bytes, so the bench scales it to
 # its own mean position by the algorithmic-bytes ratio.
-NCU_TRAFFIC_P19 = 1_197_266_432
+NCU_TRAFFIC_P19 = 1_196_995_755
 
 
 def bytes_per_token(pos: int) -> int:
