@@ -1,27 +1,44 @@
 // Causal GQA flash attention for prefill on the 5th-generation tensor cores
 // (tcgen05, accumulators in TMEM).
 //
-// One CTA = (block of 128 query rows, q head, sequence); 320 threads:
-//   warp 0      TMA producers: lane 0 loads Q once, then K tiles of 128 keys
-//               into a 3-stage ring (a stage is freed as soon as S_j is
-//               done); lane 1 loads the V^T tiles into a 2-stage ring;
+// Persistent: one CTA per SM walks a list of work items, an item being (block
+// of 128 query rows, q head, sequence).  Items are ordered heaviest (latest
+// query block) first and dealt to the CTAs in a snake order (round r gives
+// item r * G + c to CTA c, or r * G + G - 1 - c on odd rounds), so the loads
+// balance like longest-processing-time-first.  TMEM, barriers and tensor maps
+// are set up once per CTA; the rings, S/P buffers and barrier phases run on
+// per-CTA tile counters g across items.  (One CTA per item cost 3.4 us of
+// set-up, Q load and pipeline fill per item plus a 1.4 us gap before the next
+// CTA started on the SM, against 1.23 us per 128-key tile.)
+// 448 threads:
+//   warp 0      TMA producers: lane 0 loads each item's Q (once the item
+//               before has no S MMA left to run; the next item's Q and first
+//               K tile are prefetched into L2 when an item starts), then K
+//               tiles of 128 keys into a 3-stage ring (a stage is freed as
+//               soon as S_g is done); lane 1 loads the V^T tiles into a
+//               2-stage ring;
 //   warp 1      TMEM owner; one thread issues the MMAs:
-//                 S_j = Q K_j^T  (M=128 queries, N=128 keys, K=128 dims) into
+//                 S_g = Q K_g^T  (M=128 queries, N=128 keys, K=128 dims) into
 //                                 one of two S buffers,
-//                 O += P_j V_j   (M=128 queries, N=128 dims, K=128 keys),
-//                                 accumulated in TMEM across the key tiles;
-//               S_{j+1} is issued before O_j so the tensor core works while
-//               the softmax warps are busy;
-//   warps 2-9   softmax and output: warp w owns query rows 32 (w % 4) ..
-//               (its TMEM lane quadrant) and column half (w - 2) / 4 of S
-//               and O; row maxima are exchanged with the partner warp through
-//               shared memory.  exp2 of S_j in registers, P_j stored as bf16
-//               into one of two TMEM buffers, from which the P V MMA reads
-//               its A operand.  P is taken relative to the row maximum in use; O
-//               in TMEM is rescaled (tcgen05.ld / st) only when a row maximum
-//               grows by more than 2^8, so P stays below 256 and most tiles
-//               touch O not at all.  Each half keeps its own row sum, added at
-//               the end.
+//                 O += P_g V_g   (M=128 queries, N=128 dims, K=128 keys),
+//                                 accumulated in TMEM across the item's tiles;
+//               S_{g+1} is issued before PV_g so the tensor core works while
+//               the softmax warps are busy; an item's first PV waits until
+//               the output warps have read the previous item's O;
+//   warps 2-9   softmax: warp w owns query rows 32 (w % 4) .. (its TMEM lane
+//               quadrant) and column half (w - 2) / 4 of S; row maxima are
+//               exchanged with the partner warp through shared memory.  exp2
+//               of S_g in registers, P_g stored as bf16 into one of two TMEM
+//               buffers, from which the P V MMA reads its A operand.  P is
+//               taken relative to the row maximum in use; O in TMEM is
+//               rescaled (tcgen05.ld / st) only when a row maximum grows by
+//               more than 2^8, so P stays below 256 and most tiles touch O not
+//               at all.  Each half keeps its own row sum, handed to the output
+//               warps through shared memory at the end of the item;
+//   warps 10-13 output: one per TMEM lane quadrant, a thread per query row;
+//               after the item's last PV they read O, scale by 1 / row sum
+//               and store bf16, while the softmax warps are already on the
+//               next item's first tile.
 // All operands are K-major: Q [q][d], K [key][d], P [q][key] (TMEM) and V^T [d][key]
 // (the QKV GEMM epilogue writes V transposed per sequence and kv head).
 // Scores are in the log2 domain: the QKV epilogue stores q pre-multiplied by
@@ -46,9 +63,11 @@ constexpr int SM_K = SM_Q + TILE;           // [KST] stages
 constexpr int SM_V = SM_K + KST * TILE;     // [VST] stages (V^T)
 constexpr int SM_BAR = SM_V + VST * TILE;
 constexpr int SM_RED = SM_BAR + 256;        // fp32 [2 tiles][2 halves][128 rows] row maxima
-constexpr int SMEM = SM_RED + 2 * 2 * 128 * 4 + 1024;   // + barriers, row-max exchange, alignment slack
+constexpr int SM_SUM = SM_RED + 2 * 2 * 128 * 4;   // fp32 [2 items][2 halves][128 rows] row sums
+constexpr int SMEM = SM_SUM + 2 * 2 * 128 * 4 + 1024;   // + alignment slack
 constexpr int SOFT_WARPS = 8;               // two warps per TMEM lane quadrant, one per column half
-constexpr int THREADS = 64 + 32 * SOFT_WARPS;
+constexpr int EPI_WARP0 = 2 + SOFT_WARPS;   // four output warps, one per TMEM lane quadrant
+constexpr int THREADS = 64 + 32 * SOFT_WARPS + 128;
 // TMEM columns: S_j buffers at 0 / 128 (fp32), O at 256 (fp32), P_j buffers at
 // 384 / 448 (bf16 packed two per column: 128 keys = 64 columns)
 constexpr uint32_t TM_O = 256, TM_P = 384;
@@ -56,6 +75,7 @@ constexpr uint32_t TM_O = 256, TM_P = 384;
 struct Args {
     __nv_bfloat16* O;       // [M, 2048] bf16, row m = b * S + s
     int S;                  // sequence length
+    int B;                  // sequences
     // K is read straight from the layer's K cache (rows of 128): key s of kv head
     // h of sequence b is row k_row0 + b * k_seq_rows + h * k_head_rows + s
     long long k_row0, k_seq_rows, k_head_rows;
@@ -87,6 +107,21 @@ __device__ __forceinline__ bool fa_wait(uint64_t* bar, uint32_t parity, long lon
     return true;
 }
 
+// Work item `it` of CTA c among G: (q head, sequence, query block), or false
+// past the end.  Linear item k: heads fastest, then sequences, then query
+// blocks from the last (heaviest) to the first.
+struct Item {
+    int h, b, qb;
+};
+__device__ __forceinline__ bool item_of(int it, int c, int G, int B, int nqb, Item& I) {
+    const int k = it * G + ((it & 1) ? (G - 1 - c) : c);
+    if (k >= 16 * B * nqb) return false;
+    I.h = k & 15;
+    I.b = (k >> 4) % B;
+    I.qb = nqb - 1 - (k >> 4) / B;
+    return true;
+}
+
 // tmQ: Qb [M, 2048]; tmK: the K cache as rows of 128 (see Args); tmV: V^T [B * 8 * 128, ldv]
 // (rows = (b * 8 + kvh) * 128 + d).  Key rows past S (the last tile) hold other
 // cache rows or TMA zero fill; the softmax masks them.
@@ -103,25 +138,25 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     uint64_t* v_empty = bars + 9;     // [VST]
     uint64_t* s_full = bars + 11;     // [2]
     uint64_t* s_free = bars + 13;     // [2]
-    uint64_t* p_full = bars + 15;     // [2] P_j stored on p_full[j & 1] (one barrier per P buffer)
-    uint64_t* o_full = bars + 17;     // [2] PV_j completion on o_full[j & 1]
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 19);
+    uint64_t* p_full = bars + 15;     // [2] P_g stored on p_full[g & 1] (one barrier per P buffer)
+    uint64_t* o_full = bars + 17;     // [2] PV_g completion on o_full[g & 1]
+    uint64_t* q_empty = bars + 19;    // every S MMA of the current item has completed
+    uint64_t* l_full = bars + 20;     // the item's row sums are in SM_SUM[it & 1]
+    uint64_t* o_empty = bars + 21;    // the output warps have read the item's O
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
-    const int S = args.S;
+    const int S = args.S, B = args.B;
     const int nqb = (S + BQ - 1) / BQ;
-    // grid (heads, batch, query blocks): CTAs are dispatched in linear block
-    // order, so every (head, sequence) pair's heaviest (latest) query block
-    // starts before any lighter one (longest-processing-time-first).
-    const int qb = nqb - 1 - (int)blockIdx.z;
-    const int h = blockIdx.x, b = blockIdx.y, kvh = h >> 1;
-    const int q0 = qb * BQ;
-    const int nt = qb + 1;                      // key tiles 0..qb (causal)
+    const int c = blockIdx.x, G = gridDim.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long lim = args.timeout_cycles;
 
     if (threadIdx.x == 0) {
         mbar_init(q_full, 1);
+        mbar_init(q_empty, 1);
+        mbar_init(l_full, SOFT_WARPS);
+        mbar_init(o_empty, 4);
         for (int i = 0; i < KST; ++i) {
             mbar_init(&k_full[i], 1);
             mbar_init(&k_empty[i], 1);
@@ -151,194 +186,289 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
+    // Tile counters run across the CTA's items: tile g of the CTA uses K stage
+    // g % KST, V stage / S buffer / P buffer g & 1, with phases from g.
     if (warp == 0) {
-        const int row0 = b * S;
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, TILE);
-            tma_load_2d(smem + SM_Q, &tmQ, h * HD, row0 + q0, q_full);
-            tma_load_2d(smem + SM_Q + ATOM, &tmQ, h * HD + 64, row0 + q0, q_full);
-            for (int j = 0; j < nt; ++j) {
-                const int st = j % KST, u = j / KST;
-                if (u >= 1 && !fa_wait(&k_empty[st], (u - 1) & 1, lim)) {
+            int g = 0;
+            Item I;
+            for (int it = 0; item_of(it, c, G, B, nqb, I); ++it) {
+                // Q is the A operand of every S MMA of the item before
+                if (it >= 1 && !fa_wait(q_empty, (it - 1) & 1, lim)) {
                     *abort_flag = 1;
-                    atomicExch(args.err, 41);
+                    atomicExch(args.err, 45);
                     break;
                 }
                 if (*abort_flag) break;
-                uint8_t* kd = smem + SM_K + st * TILE;
-                mbar_arrive_expect_tx(&k_full[st], TILE);
-                const int krow = (int)(args.k_row0 + b * args.k_seq_rows + kvh * args.k_head_rows) + j * BK;
-                tma_load_2d(kd, &tmK, 0, krow, &k_full[st]);
-                tma_load_2d(kd + ATOM, &tmK, 64, krow, &k_full[st]);
+                const int kvh = I.h >> 1, nt = I.qb + 1;
+                mbar_arrive_expect_tx(q_full, TILE);
+                tma_load_2d(smem + SM_Q, &tmQ, I.h * HD, I.b * S + I.qb * BQ, q_full);
+                tma_load_2d(smem + SM_Q + ATOM, &tmQ, I.h * HD + 64, I.b * S + I.qb * BQ, q_full);
+                // the next item's Q and first K tile into L2: they are loaded only when this
+                // item's last S MMA completes, and from L2 that latency hides behind its softmax
+                Item N;
+                if (item_of(it + 1, c, G, B, nqb, N)) {
+                    tma_prefetch_2d(&tmQ, N.h * HD, N.b * S + N.qb * BQ);
+                    tma_prefetch_2d(&tmQ, N.h * HD + 64, N.b * S + N.qb * BQ);
+                    const int nrow = (int)(args.k_row0 + N.b * args.k_seq_rows + (N.h >> 1) * args.k_head_rows);
+                    tma_prefetch_2d(&tmK, 0, nrow);
+                    tma_prefetch_2d(&tmK, 64, nrow);
+                }
+                bool ok = true;
+                for (int j = 0; j < nt; ++j, ++g) {
+                    const int st = g % KST, u = g / KST;
+                    if (u >= 1 && !fa_wait(&k_empty[st], (u - 1) & 1, lim)) {
+                        *abort_flag = 1;
+                        atomicExch(args.err, 41);
+                        ok = false;
+                        break;
+                    }
+                    if (*abort_flag) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* kd = smem + SM_K + st * TILE;
+                    mbar_arrive_expect_tx(&k_full[st], TILE);
+                    const int krow =
+                        (int)(args.k_row0 + I.b * args.k_seq_rows + kvh * args.k_head_rows) + j * BK;
+                    tma_load_2d(kd, &tmK, 0, krow, &k_full[st]);
+                    tma_load_2d(kd + ATOM, &tmK, 64, krow, &k_full[st]);
+                }
+                if (!ok) break;
             }
         } else if (lane == 1) {
-            const int vrow = (b * 8 + kvh) * HD;
-            for (int j = 0; j < nt; ++j) {
-                const int st = j & 1, u = j >> 1;
-                if (u >= 1 && !fa_wait(&v_empty[st], (u - 1) & 1, lim)) {
-                    *abort_flag = 1;
-                    atomicExch(args.err, 44);
-                    break;
+            int g = 0;
+            Item I;
+            bool ok = true;
+            for (int it = 0; ok && item_of(it, c, G, B, nqb, I); ++it) {
+                const int vrow = (I.b * 8 + (I.h >> 1)) * HD, nt = I.qb + 1;
+                for (int j = 0; j < nt; ++j, ++g) {
+                    const int st = g & 1, u = g >> 1;
+                    if (u >= 1 && !fa_wait(&v_empty[st], (u - 1) & 1, lim)) {
+                        *abort_flag = 1;
+                        atomicExch(args.err, 44);
+                        ok = false;
+                        break;
+                    }
+                    if (*abort_flag) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t* vd = smem + SM_V + st * TILE;
+                    mbar_arrive_expect_tx(&v_full[st], TILE);
+                    tma_load_2d(vd, &tmV, j * BK, vrow, &v_full[st]);
+                    tma_load_2d(vd + ATOM, &tmV, j * BK + 64, vrow, &v_full[st]);
                 }
-                if (*abort_flag) break;
-                uint8_t* vd = smem + SM_V + st * TILE;
-                mbar_arrive_expect_tx(&v_full[st], TILE);
-                tma_load_2d(vd, &tmV, j * BK, vrow, &v_full[st]);
-                tma_load_2d(vd + ATOM, &tmV, j * BK + 64, vrow, &v_full[st]);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(BQ, BK);
             const uint32_t sq = smem_u32(smem + SM_Q);
-            bool ok = fa_wait(q_full, 0, lim);
-            // O_j = P_j V_j into the O buffer
-            auto pv = [&](int j) -> bool {
-                // P_j stored in TMEM and O rescaled (if the row maxima moved) by the softmax warps
-                if (!fa_wait(&p_full[j & 1], (j >> 1) & 1, lim)) return false;
-                if (!fa_wait(&v_full[j & 1], (j >> 1) & 1, lim)) return false;
+            // O (+)= P_g V_g; `first` starts item it's accumulator, once the output
+            // warps have read the O of item it - 1
+            auto pv = [&](int g, bool first, int it) -> bool {
+                if (first && it >= 1 && !fa_wait(o_empty, (it - 1) & 1, lim)) return false;
+                // P_g stored in TMEM and O rescaled (if the row maxima moved) by the softmax warps
+                if (!fa_wait(&p_full[g & 1], (g >> 1) & 1, lim)) return false;
+                if (!fa_wait(&v_full[g & 1], (g >> 1) & 1, lim)) return false;
                 tc_fence_after();
-                const uint32_t sv = smem_u32(smem + SM_V + (j & 1) * TILE);
-                const uint32_t pa = tmem + TM_P + (j & 1) * 64;
+                const uint32_t sv = smem_u32(smem + SM_V + (g & 1) * TILE);
+                const uint32_t pa = tmem + TM_P + (g & 1) * 64;
 #pragma unroll
                 for (int k = 0; k < HD / 16; ++k) {
                     const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
-                    tc_mma_f16_ts(tmem + TM_O, pa + k * 8, sw128_kmajor_desc(sv + off), idesc, (j | k) != 0);
+                    tc_mma_f16_ts(tmem + TM_O, pa + k * 8, sw128_kmajor_desc(sv + off), idesc, !first || k != 0);
                 }
-                tc_commit(&o_full[j & 1]);
-                tc_commit(&v_empty[j & 1]);
+                tc_commit(&o_full[g & 1]);
+                tc_commit(&v_empty[g & 1]);
                 return true;
             };
-            for (int j = 0; ok && j < nt; ++j) {
-                const int st = j & 1, u = j >> 1, kst = j % KST;
-                if (!fa_wait(&k_full[kst], (j / KST) & 1, lim) ||
-                    (u >= 1 && !fa_wait(&s_free[st], (u - 1) & 1, lim)) || *abort_flag) {
+            bool ok = true;
+            int g = 0;
+            Item I;
+            for (int it = 0; ok && item_of(it, c, G, B, nqb, I); ++it) {
+                const int nt = I.qb + 1;
+                if (!fa_wait(q_full, it & 1, lim)) {
                     ok = false;
                     break;
                 }
-                tc_fence_after();
-                const uint32_t sk = smem_u32(smem + SM_K + kst * TILE);
+                for (int j = 0; j < nt; ++j, ++g) {
+                    const int st = g & 1, u = g >> 1, kst = g % KST;
+                    if (!fa_wait(&k_full[kst], (g / KST) & 1, lim) ||
+                        (u >= 1 && !fa_wait(&s_free[st], (u - 1) & 1, lim)) || *abort_flag) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sk = smem_u32(smem + SM_K + kst * TILE);
 #pragma unroll
-                for (int k = 0; k < HD / 16; ++k) {
-                    const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
-                    tc_mma_f16(tmem + st * BK, sw128_kmajor_desc(sq + off), sw128_kmajor_desc(sk + off), idesc,
-                               k != 0);
+                    for (int k = 0; k < HD / 16; ++k) {
+                        const uint32_t off = (k >> 2) * ATOM + (k & 3) * 32;
+                        tc_mma_f16(tmem + st * BK, sw128_kmajor_desc(sq + off), sw128_kmajor_desc(sk + off), idesc,
+                                   k != 0);
+                    }
+                    tc_commit(&s_full[st]);
+                    tc_commit(&k_empty[kst]);   // K_g read: its stage can take K_{g+KST}
+                    if (j == nt - 1) tc_commit(q_empty);   // the item's last S: Q may be replaced
+                    // S_g is issued before PV_{g-1} so the tensor core works while the softmax runs
+                    if (j >= 1 && !pv(g - 1, j == 1, it)) {
+                        ok = false;
+                        break;
+                    }
                 }
-                tc_commit(&s_full[st]);
-                tc_commit(&k_empty[kst]);   // K_j read: its stage can take K_{j+KST}
-                if (j >= 1 && !pv(j - 1)) {
-                    ok = false;
-                    break;
-                }
+                // the item's last PV before the next item's Q wait: the output warps need it
+                if (ok && !pv(g - 1, nt == 1, it)) ok = false;
             }
-            if (ok && !pv(nt - 1)) ok = false;
             if (!ok) {
                 *abort_flag = 1;
                 atomicExch(args.err, 42);
             }
         }
-    } else {
-        // softmax / output: thread = (query row r, column half hh)
+    } else if (warp < EPI_WARP0) {
+        // softmax: thread = (query row r, column half hh)
         const int quad = warp & 3, hh = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
-        const int qrow = q0 + r;
         const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
         const uint32_t oa = tmem + lane_off + TM_O + hh * 64;   // this thread's half of its O row
         float* red = reinterpret_cast<float*>(smem + SM_RED);     // [2][2][128]
+        float* rsum = reinterpret_cast<float*>(smem + SM_SUM);    // [2 items][2][128]
         constexpr float RESCALE_LOG2 = 8.f;
-        float m = -INFINITY, l = 0.f;
+        // after a failed wait the loops still run to the end (without waiting) so that the
+        // partner warp's named barriers are always matched
         bool ok = true;
-        for (int j = 0; j < nt; ++j) {
-            const int st = j & 1, u = j >> 1;
-            // after a failed wait the loop still runs to the end (without waiting) so that the
-            // partner warp's named barriers are always matched
-            fa_stamp(args, j, 0);
-            if (ok && (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag)) ok = false;
-            fa_stamp(args, j, 1);
-            tc_fence_after();
-            const int k0 = j * BK + hh * 64;
-            float sv[64];
-            tmem_ld32(tmem + lane_off + st * BK + hh * 64, sv);
-            tmem_ld32(tmem + lane_off + st * BK + hh * 64 + 32, sv + 32);
-            // S buffer consumed: the MMA may compute S_{j+2} into it
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&s_free[st]);
-            fa_stamp(args, j, 2);
-            // scores are already in the log2 domain (q is stored pre-scaled); only the diagonal
-            // tile and a tile past the sequence end need the causal / length mask
-            float tmax = -INFINITY;
-            if (j == qb || (j + 1) * BK > S) {
-#pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const int key = k0 + i;
-                    sv[i] = (key > qrow || key >= S) ? -INFINITY : sv[i];
-                    tmax = fmaxf(tmax, sv[i]);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 64; ++i) tmax = fmaxf(tmax, sv[i]);
-            }
-            // row maximum over both halves (partner warp w +- 4 shares the lane quadrant)
-            red[(st * 2 + hh) * 128 + r] = tmax;
-            fa_stamp(args, j, 3);
-            named_bar_sync(1 + quad, 64);
-            tmax = fmaxf(tmax, red[(st * 2 + (hh ^ 1)) * 128 + r]);
-            fa_stamp(args, j, 4);
-            // move the row to a new maximum only when it grew by more than 2^8
-            float corr = 1.f;
-            if (tmax > m + RESCALE_LOG2) {
-                corr = ex2_approx(m - tmax);   // 0 on the first tile (m = -inf)
-                m = tmax;
-            }
-            l *= corr;
-            if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
-                // O rescale: PV_{j-1} must have completed
-                if (ok && !fa_wait(&o_full[(j - 1) & 1], ((j - 1) >> 1) & 1, lim)) ok = false;
+        int g = 0;
+        Item I;
+        for (int it = 0; item_of(it, c, G, B, nqb, I); ++it) {
+            const int qb = I.qb, nt = qb + 1;
+            const int qrow = qb * BQ + r;
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < nt; ++j, ++g) {
+                const int st = g & 1, u = g >> 1;
+                fa_stamp(args, g, 0);
+                if (ok && (!fa_wait(&s_full[st], u & 1, lim) || *abort_flag)) ok = false;
+                fa_stamp(args, g, 1);
                 tc_fence_after();
+                const int k0 = j * BK + hh * 64;
+                float sv[64];
+                tmem_ld32(tmem + lane_off + st * BK + hh * 64, sv);
+                tmem_ld32(tmem + lane_off + st * BK + hh * 64 + 32, sv + 32);
+                // S buffer consumed: the MMA may compute S_{g+2} into it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[st]);
+                fa_stamp(args, g, 2);
+                // scores are already in the log2 domain (q is stored pre-scaled); only the diagonal
+                // tile and a tile past the sequence end need the causal / length mask
+                float tmax = -INFINITY;
+                if (j == qb || (j + 1) * BK > S) {
+                    // keys k0 + i are visible for i <= last (causal and length limits in one compare)
+                    const int last = min(qrow, S - 1) - k0;
 #pragma unroll
-                for (int c = 0; c < 64; c += 32) {
-                    float v[32];
-                    tmem_ld32(oa + c, v);
+                    for (int i = 0; i < 64; ++i) {
+                        sv[i] = i > last ? -INFINITY : sv[i];
+                        tmax = fmaxf(tmax, sv[i]);
+                    }
+                } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] *= corr;
-                    tmem_st32(oa + c, v);
+                    for (int i = 0; i < 64; ++i) tmax = fmaxf(tmax, sv[i]);
                 }
-            }
-            // P_j goes to TMEM buffer j & 1, last read by PV_{j-2}
-            if (j >= 2 && ok && !fa_wait(&o_full[st], (u - 1) & 1, lim)) ok = false;
-            // P = exp2(s - m) (at most 2^8), bf16 packed in pairs: keys 64 hh .. + 63 = columns 32 hh .. + 31
-            float psum = 0.f;
-            uint32_t pk[32];
+                // row maximum over both halves (partner warp w +- 4 shares the lane quadrant)
+                red[(st * 2 + hh) * 128 + r] = tmax;
+                fa_stamp(args, g, 3);
+                named_bar_sync(1 + quad, 64);
+                tmax = fmaxf(tmax, red[(st * 2 + (hh ^ 1)) * 128 + r]);
+                fa_stamp(args, g, 4);
+                // move the row to a new maximum only when it grew by more than 2^8
+                float corr = 1.f;
+                if (tmax > m + RESCALE_LOG2) {
+                    corr = ex2_approx(m - tmax);   // 0 on the first tile (m = -inf)
+                    m = tmax;
+                }
+                l *= corr;
+                if (j >= 1 && __any_sync(0xffffffffu, corr != 1.f)) {
+                    // O rescale: PV_{g-1} must have completed
+                    if (ok && !fa_wait(&o_full[(g - 1) & 1], ((g - 1) >> 1) & 1, lim)) ok = false;
+                    tc_fence_after();
+#pragma unroll 1
+                    for (int cc = 0; cc < 64; cc += 16) {
+                        float v[16];
+                        tmem_ld16(oa + cc, v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float p0 = ex2_approx(sv[2 * i] - m), p1 = ex2_approx(sv[2 * i + 1] - m);
-                psum += p0 + p1;
-                __nv_bfloat162 t = __floats2bfloat162_rn(p0, p1);
-                pk[i] = *reinterpret_cast<uint32_t*>(&t);
+                        for (int i = 0; i < 16; ++i) v[i] *= corr;
+                        tmem_st16(oa + cc, v);
+                    }
+                }
+                // P_g goes to TMEM buffer g & 1, last read by PV_{g-2}
+                if (g >= 2 && ok && !fa_wait(&o_full[st], (u - 1) & 1, lim)) ok = false;
+                // P = exp2(s - m) (at most 2^8), bf16 packed in pairs: keys 64 hh .. + 63 = columns 32 hh .. + 31
+                // (two stores of 16 columns keep fewer packed words live)
+                float psum = 0.f;
+#pragma unroll
+                for (int hq = 0; hq < 2; ++hq) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const int e = 32 * hq + 2 * i;
+                        const float p0 = ex2_approx(sv[e] - m), p1 = ex2_approx(sv[e + 1] - m);
+                        psum += p0 + p1;
+                        __nv_bfloat162 t = __floats2bfloat162_rn(p0, p1);
+                        pk[i] = *reinterpret_cast<uint32_t*>(&t);
+                    }
+                    tmem_st16_nowait(tmem + lane_off + TM_P + st * 64 + hh * 32 + 16 * hq, pk);
+                }
+                fa_stamp(args, g, 5);
+                tmem_st_wait();
+                fa_stamp(args, g, 6);
+                l += psum;
+                // P stored and O rescale done: PV_g may start
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&p_full[st]);
             }
-            fa_stamp(args, j, 5);
-            tmem_st32_u(tmem + lane_off + TM_P + st * 64 + hh * 32, pk);
-            fa_stamp(args, j, 6);
-            l += psum;
-            // P stored and O rescale done: PV_j may start
-            tc_fence_before();
+            // this half's row sum for the output warps (the row maximum is shared).  The
+            // output warps must be past item it - 1 first: after a one-tile item nothing
+            // else keeps l_full from completing two phases ahead of their wait.
+            if (it >= 1 && ok && !fa_wait(o_empty, (it - 1) & 1, lim)) ok = false;
+            rsum[((it & 1) * 2 + hh) * 128 + r] = l;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[st]);
+            if (lane == 0) mbar_arrive(l_full);
         }
-        // both halves' row sums (same row maximum)
-        named_bar_sync(1 + quad, 64);
-        red[hh * 128 + r] = l;
-        named_bar_sync(1 + quad, 64);
-        const float ltot = l + red[(hh ^ 1) * 128 + r];
-        if (ok && fa_wait(&o_full[(nt - 1) & 1], ((nt - 1) >> 1) & 1, lim)) {
+    } else {
+        // output: thread = query row r of its TMEM lane quadrant, all 128 dims of O.
+        // Item it's O is complete when its last PV (tile g - 1) has; read, scale
+        // by 1 / row sum, store bf16, then release O to the next item's first PV.
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
+        const uint32_t oa = tmem + ((uint32_t)(quad * 32) << 16) + TM_O;
+        const float* rsum = reinterpret_cast<const float*>(smem + SM_SUM);
+        bool ok = true;
+        int g = 0;
+        Item I;
+        for (int it = 0; item_of(it, c, G, B, nqb, I); ++it) {
+            g += I.qb + 1;
+            const int qrow = I.qb * BQ + r;
+            if (ok && (!fa_wait(l_full, it & 1, lim) || !fa_wait(&o_full[(g - 1) & 1], ((g - 1) >> 1) & 1, lim) ||
+                       *abort_flag))
+                ok = false;
+            if (!ok) {
+                if (lane == 0) atomicExch(args.err, 43);
+                *abort_flag = 1;
+                break;
+            }
             tc_fence_after();
-            const float inv = 1.f / ltot;
-            __nv_bfloat16* out = args.O + ((size_t)b * S + qrow) * 2048 + h * HD + hh * 64;
+            const float inv = 1.f / (rsum[((it & 1) * 2) * 128 + r] + rsum[((it & 1) * 2 + 1) * 128 + r]);
+            __nv_bfloat16* out = args.O + ((size_t)I.b * S + qrow) * 2048 + I.h * HD;
 #pragma unroll
-            for (int c = 0; c < 64; c += 32) {
+            for (int cc = 0; cc < HD; cc += 32) {
                 float v[32];
-                tmem_ld32(oa + c, v);
+                tmem_ld32(oa + cc, v);
+                if (cc == HD - 32) {
+                    // every O column read: the next item's first PV may overwrite it
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(o_empty);
+                }
                 if (qrow < S) {
 #pragma unroll
                     for (int i = 0; i < 32; i += 8) {
@@ -351,13 +481,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                         pk.y = *reinterpret_cast<uint32_t*>(&b1);
                         pk.z = *reinterpret_cast<uint32_t*>(&b2);
                         pk.w = *reinterpret_cast<uint32_t*>(&b3);
-                        *reinterpret_cast<uint4*>(out + c + i) = pk;
+                        *reinterpret_cast<uint4*>(out + cc + i) = pk;
                     }
                 }
             }
-        } else {
-            if (lane == 0) atomicExch(args.err, 43);
-            *abort_flag = 1;
         }
     }
     tc_fence_before();

@@ -325,6 +325,7 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             fa::Args fa_args;
             fa_args.O = Ob;
             fa_args.S = S;
+            fa_args.B = B;
             fa_args.k_row0 = (long long)l * MQ_NUM_KV_HEADS * head_rows;
             fa_args.k_seq_rows = seq_rows;
             fa_args.k_head_rows = head_rows;
@@ -342,7 +343,9 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
                 }
             }
 #endif
-            dim3 fgrid(MQ_NUM_Q_HEADS, B, (S + fa::BQ - 1) / fa::BQ);
+            // persistent: one CTA per SM over (q head, sequence, query block) items
+            const int items = MQ_NUM_Q_HEADS * B * ((S + fa::BQ - 1) / fa::BQ);
+            const int fgrid = items < num_sms() ? items : num_sms();
             fa::fa_tc_kernel<<<fgrid, fa::THREADS, fa::SMEM, st>>>(tmQ, tmK, tmV, fa_args);
         }
         MQ_TRY(gemm_bf16(Ob, 2048, W.o_proj_weight, 2048, nullptr, X, 1024, M, 1024, 2048, EPI_ADD_F32, err, st));
