@@ -11,19 +11,19 @@
 // set-up, Q load and pipeline fill per item plus a 1.4 us gap before the next
 // CTA started on the SM, against 1.23 us per 128-key tile.)
 // 448 threads:
-//   warp 0      TMA producers: lane 0 loads each item's Q (once the item
-//               before has no S MMA left to run; the next item's Q and first
-//               K tile are prefetched into L2 when an item starts), then K
-//               tiles of 128 keys into a 3-stage ring (a stage is freed as
-//               soon as S_g is done); lane 1 loads the V^T tiles into a
-//               2-stage ring;
+//   warp 0      TMA producers: lane 0 loads each item's Q into buffer it & 1
+//               (once item it - 2 has no S MMA left to run; the next item's
+//               Q and first K tile are prefetched into L2 when an item
+//               starts), then K tiles of 128 keys into a 2-stage ring (a
+//               stage is freed as soon as S_g is done); lane 1 loads the V^T
+//               tiles into a 2-stage ring;
 //   warp 1      TMEM owner; one thread issues the MMAs:
 //                 S_g = Q K_g^T  (M=128 queries, N=128 keys, K=128 dims) into
 //                                 one of two S buffers,
 //                 O += P_g V_g   (M=128 queries, N=128 dims, K=128 keys),
 //                                 accumulated in TMEM across the item's tiles;
-//               S_{g+1} is issued before PV_g so the tensor core works while
-//               the softmax warps are busy; an item's first PV waits until
+//               S_{g+1} is issued before PV_g, across items too, so the
+//               tensor core works while the softmax warps are busy; an item's first PV waits until
 //               the output warps have read the previous item's O;
 //   warps 2-9   softmax: warp w owns query rows 32 (w % 4) .. (its TMEM lane
 //               quadrant) and column half (w - 2) / 4 of S; row maxima are
@@ -57,9 +57,9 @@ constexpr int BK = 128;                     // keys per tile
 constexpr int HD = 128;                     // head dim
 constexpr int ATOM = 128 * 128;             // bytes of a 128-row x 64-element swizzled atom (16 KB)
 constexpr int TILE = 2 * ATOM;              // a 128 x 128 bf16 operand (32 KB)
-constexpr int SM_Q = 0;
-constexpr int KST = 3, VST = 2;             // K and V^T ring depths (separate rings: K is freed after S_j)
-constexpr int SM_K = SM_Q + TILE;           // [KST] stages
+constexpr int SM_Q = 0;                     // [2] Q buffers (item it uses it & 1)
+constexpr int KST = 2, VST = 2;             // K and V^T ring depths (separate rings: K is freed after S_g)
+constexpr int SM_K = SM_Q + 2 * TILE;       // [KST] stages
 constexpr int SM_V = SM_K + KST * TILE;     // [VST] stages (V^T)
 constexpr int SM_BAR = SM_V + VST * TILE;
 constexpr int SM_RED = SM_BAR + 256;        // fp32 [2 tiles][2 halves][128 rows] row maxima
@@ -131,8 +131,8 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     extern __shared__ uint8_t fa_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
-    uint64_t* q_full = bars + 0;
-    uint64_t* k_full = bars + 1;      // [KST]
+    uint64_t* q_full = bars + 0;      // [2]
+    uint64_t* k_full = bars + 2;      // [KST]
     uint64_t* k_empty = bars + 4;     // [KST]
     uint64_t* v_full = bars + 7;      // [VST]
     uint64_t* v_empty = bars + 9;     // [VST]
@@ -140,10 +140,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     uint64_t* s_free = bars + 13;     // [2]
     uint64_t* p_full = bars + 15;     // [2] P_g stored on p_full[g & 1] (one barrier per P buffer)
     uint64_t* o_full = bars + 17;     // [2] PV_g completion on o_full[g & 1]
-    uint64_t* q_empty = bars + 19;    // every S MMA of the current item has completed
-    uint64_t* l_full = bars + 20;     // the item's row sums are in SM_SUM[it & 1]
-    uint64_t* o_empty = bars + 21;    // the output warps have read the item's O
-    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 22);
+    uint64_t* q_empty = bars + 19;    // [2] every S MMA of the item using that Q buffer has completed
+    uint64_t* l_full = bars + 21;     // the item's row sums are in SM_SUM[it & 1]
+    uint64_t* o_empty = bars + 22;    // the output warps have read the item's O
+    uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 23);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
     const int S = args.S, B = args.B;
@@ -153,8 +153,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     const long long lim = args.timeout_cycles;
 
     if (threadIdx.x == 0) {
-        mbar_init(q_full, 1);
-        mbar_init(q_empty, 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&q_full[i], 1);
+            mbar_init(&q_empty[i], 1);
+        }
         mbar_init(l_full, SOFT_WARPS);
         mbar_init(o_empty, 4);
         for (int i = 0; i < KST; ++i) {
@@ -193,19 +195,21 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
             int g = 0;
             Item I;
             for (int it = 0; item_of(it, c, G, B, nqb, I); ++it) {
-                // Q is the A operand of every S MMA of the item before
-                if (it >= 1 && !fa_wait(q_empty, (it - 1) & 1, lim)) {
+                // Q buffer it & 1 is the A operand of every S MMA of item it - 2
+                const int qs = it & 1;
+                if (it >= 2 && !fa_wait(&q_empty[qs], ((it >> 1) - 1) & 1, lim)) {
                     *abort_flag = 1;
                     atomicExch(args.err, 45);
                     break;
                 }
                 if (*abort_flag) break;
                 const int kvh = I.h >> 1, nt = I.qb + 1;
-                mbar_arrive_expect_tx(q_full, TILE);
-                tma_load_2d(smem + SM_Q, &tmQ, I.h * HD, I.b * S + I.qb * BQ, q_full);
-                tma_load_2d(smem + SM_Q + ATOM, &tmQ, I.h * HD + 64, I.b * S + I.qb * BQ, q_full);
-                // the next item's Q and first K tile into L2: they are loaded only when this
-                // item's last S MMA completes, and from L2 that latency hides behind its softmax
+                uint8_t* qd = smem + SM_Q + qs * TILE;
+                mbar_arrive_expect_tx(&q_full[qs], TILE);
+                tma_load_2d(qd, &tmQ, I.h * HD, I.b * S + I.qb * BQ, &q_full[qs]);
+                tma_load_2d(qd + ATOM, &tmQ, I.h * HD + 64, I.b * S + I.qb * BQ, &q_full[qs]);
+                // the next item's Q and first K tile into L2 (loaded a few tiles before this
+                // item ends)
                 Item N;
                 if (item_of(it + 1, c, G, B, nqb, N)) {
                     tma_prefetch_2d(&tmQ, N.h * HD, N.b * S + N.qb * BQ);
@@ -264,7 +268,6 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     } else if (warp == 1) {
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_bf16_f32(BQ, BK);
-            const uint32_t sq = smem_u32(smem + SM_Q);
             // O (+)= P_g V_g; `first` starts item it's accumulator, once the output
             // warps have read the O of item it - 1
             auto pv = [&](int g, bool first, int it) -> bool {
@@ -284,15 +287,20 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                 tc_commit(&v_empty[g & 1]);
                 return true;
             };
+            // PV_{g-1} is issued after S_g, across item boundaries too: the next item's first
+            // S MMAs (its Q is double-buffered) run while the softmax finishes the last tile.
             bool ok = true;
             int g = 0;
+            int pg = -1, pit = 0;   // the tile whose PV is pending, its item
+            bool pfirst = false;
             Item I;
             for (int it = 0; ok && item_of(it, c, G, B, nqb, I); ++it) {
-                const int nt = I.qb + 1;
-                if (!fa_wait(q_full, it & 1, lim)) {
+                const int nt = I.qb + 1, qs = it & 1;
+                if (!fa_wait(&q_full[qs], (it >> 1) & 1, lim)) {
                     ok = false;
                     break;
                 }
+                const uint32_t sq = smem_u32(smem + SM_Q + qs * TILE);
                 for (int j = 0; j < nt; ++j, ++g) {
                     const int st = g & 1, u = g >> 1, kst = g % KST;
                     if (!fa_wait(&k_full[kst], (g / KST) & 1, lim) ||
@@ -310,16 +318,18 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
                     }
                     tc_commit(&s_full[st]);
                     tc_commit(&k_empty[kst]);   // K_g read: its stage can take K_{g+KST}
-                    if (j == nt - 1) tc_commit(q_empty);   // the item's last S: Q may be replaced
+                    if (j == nt - 1) tc_commit(&q_empty[qs]);   // the item's last S: its Q buffer is free
                     // S_g is issued before PV_{g-1} so the tensor core works while the softmax runs
-                    if (j >= 1 && !pv(g - 1, j == 1, it)) {
+                    if (pg >= 0 && !pv(pg, pfirst, pit)) {
                         ok = false;
                         break;
                     }
+                    pg = g;
+                    pfirst = j == 0;
+                    pit = it;
                 }
-                // the item's last PV before the next item's Q wait: the output warps need it
-                if (ok && !pv(g - 1, nt == 1, it)) ok = false;
             }
+            if (ok && pg >= 0 && !pv(pg, pfirst, pit)) ok = false;
             if (!ok) {
                 *abort_flag = 1;
                 atomicExch(args.err, 42);
