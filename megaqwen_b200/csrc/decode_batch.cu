@@ -622,6 +622,43 @@ int decode_batch(const mq_decode_batch_params* p, cudaStream_t st) {
 
 size_t decode_batch_workspace_bytes(int batch, int max_seq_len) { return db::layout(batch, max_seq_len).total; }
 
+namespace db {
+// tokens[b] from the LM head's 64-bit keys (value key << 32 | ~index).
+__global__ void tokens_from_keys_kernel(const unsigned long long* __restrict__ best, int* __restrict__ tokens, int B) {
+    pdl_wait();
+    pdl_trigger();
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) tokens[b] = (int)(0xffffffffu - (uint32_t)(best[b] & 0xffffffffull));
+}
+}  // namespace db
+
+// Tied LM head and greedy argmax of B <= 128 already-normalized rows (the
+// prefill's last positions): x is bf16 [lm_head_rows(B), 1024], rows past B
+// allocated but unused; logits (fp32 [B, vocab]) are written only if non-null;
+// best is B 64-bit words of scratch.  The small-batch GEMM streams the
+// embedding once with the (value, lowest index) maximum fused into its epilogue.
+int lm_head_rows(int B) { return db::np_of(B); }
+int lm_head_argmax(const void* lm_head, const void* x, int B, float* logits, unsigned long long* best, int* tokens,
+                   int* err, cudaStream_t st) {
+    using namespace db;
+    if (B < 1 || B > 128) return MQ_ERR_INVALID_ARGUMENT;
+    if (cudaMemsetAsync(best, 0, (size_t)B * sizeof(unsigned long long), st) != cudaSuccess) return MQ_ERR_CUDA;
+    const void* wl[1] = {lm_head};
+    const int nl[1] = {MQ_VOCAB_SIZE};
+    Small2Args a = {};
+    a.Bv = B;
+    a.err = err;
+    a.out = logits;
+    a.ldo = MQ_VOCAB_SIZE;
+    a.best = best;
+    a.ss_in = nullptr;
+    const int rc = small_gemm<SM_ARGMAX>(wl, nl, 1, 1024, x, np_of(B), a, st);
+    if (rc) return rc;
+    const cudaError_t e = launch(tokens_from_keys_kernel, dim3(1), dim3(128), 0, st, (const unsigned long long*)best,
+                                 tokens, B);
+    return e == cudaSuccess ? MQ_OK : note_cuda(e, "lm head argmax");
+}
+
 }  // namespace mq
 
 extern "C" {

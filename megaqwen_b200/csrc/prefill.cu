@@ -215,12 +215,17 @@ extern "C" int mq_gemm_bf16(const void* A, int lda, const void* B, int ldb, cons
 #include "attn_tc.cuh"
 
 namespace mq {
+// LM head + argmax of the last positions (small-batch GEMM, decode_batch.cu)
+int lm_head_rows(int B);
+int lm_head_argmax(const void* lm_head, const void* x, int B, float* logits, unsigned long long* best, int* tokens,
+                   int* err, cudaStream_t st);
+
 namespace {
 
 unsigned long long* g_fa_trace = nullptr;
 
 struct PrefillLayout {
-    size_t X, Xn, Qb, Vt, Ob, act, lastn, logits, err, total;
+    size_t X, Xn, Qb, Vt, Ob, act, lastn, logits, part, err, total;
 };
 
 PrefillLayout prefill_layout(int B, int S) {
@@ -234,8 +239,9 @@ PrefillLayout prefill_layout(int B, int S) {
     L.Vt = take((size_t)B * 8 * 128 * ((S + 7) / 8 * 8) * 2);   // V^T per (sequence, kv head), rows padded to 8
     L.Ob = take(M * 2048 * 2);
     L.act = take(M * 3072 * 2);
-    L.lastn = take((size_t)B * 1024 * 2);
+    L.lastn = take((size_t)(B > 128 ? B : lm_head_rows(B)) * 1024 * 2);   // LM-head operand rows (padded)
     L.logits = take((size_t)B * MQ_VOCAB_SIZE * 4);
+    L.part = take((size_t)B * pf::ARGMAX_SPLIT * 8);
     L.err = take(256);
     L.total = o;
     return L;
@@ -357,9 +363,17 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
     }
     // last position of each sequence: final norm, tied LM head, argmax
     pf::rmsnorm_bf16_kernel<<<(B + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)p->final_norm, lastn, B, S, S - 1);
+    if (B <= 128) {
+        // small-batch GEMM with the argmax fused (streams the embedding at close to the HBM rate)
+        MQ_TRY(lm_head_argmax(p->lm_head, lastn, B, p->logits, (unsigned long long*)(ws + L.part), p->out_tokens,
+                              err, st));
+        return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+    }
     MQ_TRY(gemm_bf16(lastn, 1024, p->lm_head, 1024, nullptr, logits, MQ_VOCAB_SIZE, B, MQ_VOCAB_SIZE, 1024,
                      EPI_STORE_F32, err, st));
-    pf::argmax_kernel<<<B, 1024, 0, st>>>(logits, MQ_VOCAB_SIZE, MQ_VOCAB_SIZE, p->out_tokens);
+    pf::argmax_part_kernel<<<dim3(B, pf::ARGMAX_SPLIT), 256, 0, st>>>(logits, MQ_VOCAB_SIZE, MQ_VOCAB_SIZE,
+                                                                       (float2*)(ws + L.part));
+    pf::argmax_final_kernel<<<B, pf::ARGMAX_SPLIT, 0, st>>>((const float2*)(ws + L.part), p->out_tokens);
     return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
 }
 

@@ -86,33 +86,56 @@ static __global__ void rmsnorm_bf16_kernel(const float* __restrict__ X, const bf
     }
 }
 
-// tokens[r] = lowest index of the maximum of logits[r, :V]; logits_ld elements per row.
-static __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int V, int logits_ld,
-                                                      int* __restrict__ tokens) {
-    pdl_wait();
-    pdl_trigger();
-    const float* x = logits + (size_t)blockIdx.x * logits_ld;
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = x[i];
-        if (v > best || (v == best && i < bi)) { best = v; bi = i; }
-    }
+// Greedy argmax of each sequence's logits row in two launches (one block per
+// sequence over 151,936 logits took ~74 us): argmax_part_kernel, grid
+// (sequences, ARGMAX_SPLIT), leaves each chunk's (value, index) best in
+// `part`; argmax_final_kernel, one block per sequence, reduces them.  The
+// order is (larger value, then lower index) in both stages, so the result is
+// the first index of the row maximum, as a one-pass scan gives; NaN never wins.
+constexpr int ARGMAX_SPLIT = 64;
+
+__device__ __forceinline__ void argmax_take(float& best, int& bi, float v, int i) {
+    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
+}
+
+__device__ __forceinline__ void argmax_block(float& best, int& bi) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, o);
         const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        argmax_take(best, bi, ov, oi);
     }
     __shared__ float sv[32];
     __shared__ int si[32];
     if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
-            if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
-        tokens[blockIdx.x] = bi;
-    }
+    if (threadIdx.x == 0)
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w) argmax_take(best, bi, sv[w], si[w]);
+}
+
+static __global__ void __launch_bounds__(256) argmax_part_kernel(const float* __restrict__ logits, int V,
+                                                                 int logits_ld, float2* __restrict__ part) {
+    pdl_wait();
+    pdl_trigger();
+    const float* x = logits + (size_t)blockIdx.x * logits_ld;
+    const int a = (int)(((long long)blockIdx.y * V) / ARGMAX_SPLIT);
+    const int e = (int)(((long long)(blockIdx.y + 1) * V) / ARGMAX_SPLIT);
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = a + threadIdx.x; i < e; i += blockDim.x) argmax_take(best, bi, x[i], i);
+    argmax_block(best, bi);
+    if (threadIdx.x == 0) part[blockIdx.x * ARGMAX_SPLIT + blockIdx.y] = make_float2(best, __int_as_float(bi));
+}
+
+static __global__ void __launch_bounds__(ARGMAX_SPLIT) argmax_final_kernel(const float2* __restrict__ part,
+                                                                           int* __restrict__ tokens) {
+    pdl_wait();
+    pdl_trigger();
+    const float2 p = part[blockIdx.x * ARGMAX_SPLIT + threadIdx.x];
+    float best = p.x;
+    int bi = __float_as_int(p.y);
+    argmax_block(best, bi);
+    if (threadIdx.x == 0) tokens[blockIdx.x] = bi;
 }
 
 }  // namespace pf
