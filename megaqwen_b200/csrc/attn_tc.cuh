@@ -187,6 +187,10 @@ fa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CU
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    // Programmatic dependent launch: the set-up above overlapped the previous
+    // kernel's tail; nothing it wrote is read before pdl_wait.
+    pdl_trigger();
+    pdl_wait();
 
     // Tile counters run across the CTA's items: tile g of the CTA uses K stage
     // g % KST, V stage / S buffer / P buffer g & 1, with phases from g.

@@ -144,6 +144,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     pair_sync();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    // Programmatic dependent launch: the set-up above overlapped the previous
+    // kernel's tail; nothing it wrote is read before pdl_wait.
+    pdl_trigger();
+    pdl_wait();
     const uint32_t full_leader = pair_mapa(smem_u32(full), 0);
     const uint32_t acce_leader = pair_mapa(smem_u32(acce), 0);
 

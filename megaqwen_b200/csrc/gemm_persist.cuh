@@ -225,6 +225,10 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
+    // Programmatic dependent launch: the set-up above overlapped the previous
+    // kernel's tail; nothing it wrote is read before pdl_wait.
+    pdl_trigger();
+    pdl_wait();
 
     if (warp == 0) {
         if (lane == 0) {

@@ -58,6 +58,25 @@ int num_sms() {
     return sms[dev] > 0 ? sms[dev] : 148;
 }
 
+// Launch as a programmatic dependent of the previous kernel in the stream (the
+// GEMMs and the attention call pdl_wait after their set-up: barrier init, TMEM
+// allocation, tensor-map prefetch), so that set-up overlaps the previous tail.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // One persistent GEMM launch: A [M, K] against up to three B maps side by side
 // (Nmap[i] rows each; EPI_SILU_MUL: gate, up), one CTA per SM, BN-wide tiles.
 template <int EPI, int BN>
@@ -93,8 +112,9 @@ int launch_persist_bn(const void* A, int lda, const void* const* Bm, const int* 
     a.timeout_cycles = 4000000000ll;  // ~2 s at 1.9 GHz
     const int ntiles = a.tiles_m * a.tiles_n;
     const int grid = ntiles < num_sms() ? ntiles : num_sms();
-    gemm_persist_kernel<EPI, BN><<<grid, P_THREADS, Cfg::SMEM, stream>>>(ta, tb[0], tb[1], tb[2], a);
-    return cudaGetLastError() == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
+    const cudaError_t e = launch_pdl(gemm_persist_kernel<EPI, BN>, dim3(grid), dim3(P_THREADS), (size_t)Cfg::SMEM,
+                                     stream, ta, tb[0], tb[1], tb[2], a);
+    return e == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
 }
 
 // 256-wide tiles where every B map's rows allow them (gate/up keep 128: two accumulators)
@@ -150,13 +170,15 @@ int launch_pair(const void* A, int lda, const void* B, const void* B2, int ldb, 
     cfg.blockDim = dim3(P_THREADS);
     cfg.dynamicSmemBytes = PAIR_SMEM;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 2;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_pair_kernel<EPI>, ta, tb0, tb1, a);
     return e == cudaSuccess ? MQ_OK : MQ_ERR_CUDA;
 }
@@ -304,6 +326,8 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
     pf::embed_kernel<<<(M + 7) / 8, 256, 0, st>>>(p->ids, (const pf::bf16*)p->embed, X, M);
     for (int l = 0; l < p->num_layers; ++l) {
         const LDGLayerWeights& W = p->layers_host[l];
+        // the norms are plain launches: as programmatic dependents their blocks sat
+        // resident through the preceding GEMM, and B = 8 was 3 % slower
         pf::rmsnorm_bf16_kernel<<<(M + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)W.input_layernorm_weight, Xn, M, 1, 0);
         {
             // q | k | v projections with QK-norm, RoPE and the K/V cache write in the epilogue
@@ -352,7 +376,9 @@ int prefill_forward(const mq_prefill_params* p, cudaStream_t st) {
             // persistent: one CTA per SM over (q head, sequence, query block) items
             const int items = MQ_NUM_Q_HEADS * B * ((S + fa::BQ - 1) / fa::BQ);
             const int fgrid = items < num_sms() ? items : num_sms();
-            fa::fa_tc_kernel<<<fgrid, fa::THREADS, fa::SMEM, st>>>(tmQ, tmK, tmV, fa_args);
+            if (launch_pdl(fa::fa_tc_kernel, dim3(fgrid), dim3(fa::THREADS), (size_t)fa::SMEM, st, tmQ, tmK, tmV,
+                           fa_args) != cudaSuccess)
+                return MQ_ERR_CUDA;
         }
         MQ_TRY(gemm_bf16(Ob, 2048, W.o_proj_weight, 2048, nullptr, X, 1024, M, 1024, 2048, EPI_ADD_F32, err, st));
         pf::rmsnorm_bf16_kernel<<<(M + 7) / 8, 256, 0, st>>>(X, (const pf::bf16*)W.post_attn_layernorm_weight, Xn, M,
