@@ -327,20 +327,31 @@ gemm_persist_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                 // one round of coalesced loads instead of dependent per-row loads in
                 // the epilogue.  The partner warp of the quadrant is done with the
                 // previous tile's rows at the first barrier.
-                named_bar_sync(1 + quad, 64);
+                // All 16 loads of a lane are issued before the barrier and stored after it, so
+                // the tile pays one load latency, overlapped with the wait for the partner warp
+                // (with four loads in flight at a time, four loaded-L2 round trips per tile sat
+                // on the epilogue's path).
                 const int mt = (t / args.tiles_n) * GEMM_BM;
                 const bool is_v = (t % args.tiles_n) >= args.nb0 + args.nb1;
+                uint4 rows[16];
                 if (!is_v) {
                     const __nv_bfloat16* tab = half ? args.qkv.sin_table : args.qkv.cos_table;
-                    __nv_bfloat16* dst = rope + (size_t)(half * GEMM_BM + quad * 32) * 128;
-#pragma unroll 4
-                    for (int i = lane; i < 32 * 16; i += 32) {
-                        const int r = i >> 4, ch = i & 15;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const int i = lane + 32 * k, r = i >> 4, ch = i & 15;
                         const int grow = mt + quad * 32 + r;
                         const int gr = grow < args.M ? grow : 0;
                         const int pp = args.qkv.start_pos + gr % args.qkv.S;
-                        *reinterpret_cast<uint4*>(dst + r * 128 + ((ch ^ (r & 15)) * 8)) =
-                            *reinterpret_cast<const uint4*>(tab + (size_t)pp * 128 + ch * 8);
+                        rows[k] = *reinterpret_cast<const uint4*>(tab + (size_t)pp * 128 + ch * 8);
+                    }
+                }
+                named_bar_sync(1 + quad, 64);
+                if (!is_v) {
+                    __nv_bfloat16* dst = rope + (size_t)(half * GEMM_BM + quad * 32) * 128;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const int i = lane + 32 * k, r = i >> 4, ch = i & 15;
+                        *reinterpret_cast<uint4*>(dst + r * 128 + ((ch ^ (r & 15)) * 8)) = rows[k];
                     }
                 }
             }
