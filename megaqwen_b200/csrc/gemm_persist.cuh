@@ -140,7 +140,7 @@ __device__ __forceinline__ void qkv_row_epilogue(const PArgs& a, uint32_t acc, i
     const float osc = map == 0 ? e.q_scale : 1.f;
     // rotate-half pairs (d, d + 64): chunk c with chunk c + 64; weights, cos and
     // sin rows are read 8 bf16 at a time
-#pragma unroll 1
+#pragma unroll
     for (int c = 0; c < 64; c += 32) {
         float x1[32], x2[32];
         tmem_ld32(acc + c, x1);
