@@ -66,6 +66,41 @@ def test_prefill_batch_matches_single_sequences():
         assert torch.equal(dec.get_k_cache()[:, :, :S], kc[b, :, :, :S])
 
 
+def test_prefill_batch_above_128_sequences():
+    """Batches above 128 sequences take the fp32-logits LM-head GEMM and the
+    two-stage argmax (64 blocks per sequence, then one reduction block); up to
+    128 the small-batch GEMM with the argmax fused.  A 130-sequence batch
+    against the same prompts in batches of 128 and 2: logits agree, and each
+    path's tokens are the first index of its own row maximum."""
+    import megaqwen_b200
+    from megaqwen_b200.weights import rope_tables, seeded_prompt
+    L, S, B, MS = 1, 16, 130, 32
+    _, wd = dev_weights(L)
+    cos, sin = rope_tables(MS, device="cuda")
+    ids = torch.stack([seeded_prompt(S, seed=300 + b) for b in range(B)]).cuda()
+
+    def run(rows):
+        n = len(rows)
+        kc = torch.zeros(n, L, 8, MS, 128, dtype=torch.bfloat16, device="cuda")
+        vc = torch.zeros_like(kc)
+        lg = torch.empty(n, 151936, device="cuda")
+        tk = megaqwen_b200._C.prefill_batch(wd.embed, wd.layer_weights_flat(), wd.final_norm, wd.lm_head, cos, sin,
+                                            ids[rows].contiguous(), kc, vc, lg)
+        torch.cuda.synchronize()
+        return tk.cpu(), lg
+
+    big_t, big_l = run(list(range(B)))
+    small = [run(list(range(128))), run([128, 129])]
+    small_t = torch.cat([t for t, _ in small])
+    small_l = torch.cat([lg for _, lg in small])
+    assert (big_l - small_l).abs().max().item() < 1e-3
+    assert torch.equal(big_t, torch.argmax(big_l, dim=1).cpu().to(big_t.dtype))
+    assert torch.equal(small_t, torch.argmax(small_l, dim=1).cpu().to(small_t.dtype))
+    top2 = torch.topk(small_l, 2, dim=1).values
+    clear = (top2[:, 0] - top2[:, 1]).cpu() > 1e-3
+    assert torch.equal(big_t[clear], small_t[clear])
+
+
 def test_config4_shape_batch8():
     """BASELINE config 4 shape on 2 layers: batch 8, prompt 2048, then decode."""
     import megaqwen_b200
